@@ -1,0 +1,222 @@
+/*
+ * microinfer_b200.h - C ABI of the B200 (sm_100a) paged KV-cache hot path.
+ *
+ * Every entry point takes raw device pointers, element counts and a
+ * cudaStream_t passed as `void*`; none allocates or frees memory.  Callers
+ * own the KV pool, the outputs and any workspace.  All work is enqueued on
+ * the given stream with no host synchronisation, so every entry point can be
+ * captured into a CUDA graph.
+ *
+ * Return value: 0 on success, a negative MI_ERR_* code when an argument is
+ * rejected (nothing was launched; mi_last_error() has the reason), or a
+ * positive cudaError_t value when a launch failed.
+ *
+ * Device status word: most kernels take an optional `int32_t *dev_status`
+ * (device memory, may be NULL).  A kernel that meets a block id outside the
+ * pool, a slot outside the cache, or a bounded wait that ran out ORs one of
+ * the MI_DEV_* bits into it and skips the offending access instead of
+ * touching memory it does not own.
+ *
+ * Layouts (row-major, innermost last):
+ *   key_cache / value_cache  [num_blocks, block_size, num_kv_heads, head_dim]
+ *   query / out              [tokens, num_q_heads, head_dim]
+ *   block_tables             int32 [num_seqs, block_table_stride], -1 padded;
+ *                            kernels never read past a row's stride
+ *   context_lens             int32 [num_seqs], includes the token just stored
+ *   cu_seqlens_q/k           int32 [num_seqs + 1], cumulative (k: contexts)
+ */
+#ifndef MICROINFER_B200_H
+#define MICROINFER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MI_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define MI_API __attribute__((visibility("default")))
+#else
+#define MI_API
+#endif
+
+/* element dtypes */
+#define MI_DTYPE_FLOAT32 0
+#define MI_DTYPE_FLOAT16 1
+#define MI_DTYPE_BFLOAT16 2
+
+/* index dtypes for slot / block / offset vectors */
+#define MI_INDEX_INT32 0
+#define MI_INDEX_INT64 1
+
+/* host-side status codes */
+#define MI_OK 0
+#define MI_ERR_INVALID (-1)     /* shape, dtype, stride or range violation  */
+#define MI_ERR_UNSUPPORTED (-2) /* valid input this build has no kernel for */
+#define MI_ERR_ALIGNMENT (-3)   /* pointer or stride not 16-byte aligned    */
+
+/* device status bits */
+#define MI_DEV_BAD_BLOCK 1 /* block id outside [0, num_blocks)     */
+#define MI_DEV_BAD_SLOT 2  /* slot outside [-1, num_blocks*bs)      */
+#define MI_DEV_TIMEOUT 4   /* a bounded mbarrier/flag wait ran out  */
+
+/* Version of this ABI (MI_ABI_VERSION). */
+MI_API int mi_abi_version(void);
+
+/* Reason for the last negative status returned on this host thread. */
+MI_API const char *mi_last_error(void);
+
+/* Number of SMs of `device` (used by the split policy), or a negative status. */
+MI_API int mi_device_sm_count(int device);
+
+/*
+ * store_kvcache: cache[blocks[t], offsets[t], h, :] = keys[t, h, :] (same
+ * for values) for every token t.  Replaces the Triton `store_kv` launcher,
+ * microinfer/worker/triton_kv_store.py:45-78 (kernel :17-41), as called by
+ * LayerKVCache.write_fast, microinfer/worker/kv_cache.py:52-79.
+ * keys/values rows may have any token stride (in elements) but each
+ * [num_kv_heads, head_dim] row must be contiguous.  Caller guarantees
+ * unique destinations (the reference's fast-path contract); ids outside the
+ * pool are skipped and flagged with MI_DEV_BAD_SLOT.
+ */
+MI_API int mi_store_kv(void *key_cache, void *value_cache, int64_t num_blocks,
+                int32_t block_size, int32_t num_kv_heads, int32_t head_dim,
+                int32_t dtype, const void *blocks, const void *offsets,
+                int32_t index_dtype, const void *keys, const void *values,
+                int64_t key_token_stride, int64_t value_token_stride,
+                int64_t num_tokens, int32_t *dev_status, void *stream);
+
+/*
+ * store_kvcache from flat slot ids (block * block_size + offset), splitting
+ * the slot on the device; slot -1 is padding and writes nothing.  Replaces
+ * the write in LayerKVCache.write_checked (microinfer/worker/kv_cache.py:30-50,
+ * host validation stays in the caller) together with the per-step slot split
+ * AttentionMetadata.slot_indices (microinfer/layer/metadata.py:75-84).
+ */
+MI_API int mi_store_kv_slots(void *key_cache, void *value_cache, int64_t num_blocks,
+                      int32_t block_size, int32_t num_kv_heads,
+                      int32_t head_dim, int32_t dtype, const void *slots,
+                      int32_t index_dtype, const void *keys, const void *values,
+                      int64_t key_token_stride, int64_t value_token_stride,
+                      int64_t num_tokens, int32_t *dev_status, void *stream);
+
+/*
+ * Split-K decode workspace size in bytes for `num_splits` splits (0 when
+ * num_splits == 1: the single-split kernel writes `out` directly).
+ */
+MI_API size_t mi_paged_decode_workspace_bytes(int64_t num_seqs, int32_t num_q_heads,
+                                       int32_t head_dim, int32_t num_splits);
+
+/*
+ * Split count the decode launcher uses when the caller passes num_splits=0:
+ * enough (seq, kv-head, split) CTAs to fill every SM twice, capped so each
+ * split keeps >= 2 key chunks when `max_context_hint` > 0 is known.
+ */
+MI_API int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads,
+                                   int32_t max_context_hint, int device);
+
+/*
+ * Paged decode attention, one query token per sequence:
+ *   out[s, h] = softmax(scale * K_s q[s, h]) V_s
+ * over the context_lens[s] cached positions found through block_tables[s],
+ * with GQA kv head h / (num_q_heads / num_kv_heads).  Replaces
+ * triton_paged_decode + _paged_decode_kernel + _paged_decode_reduce_kernel,
+ * microinfer/layer/triton_paged_attention.py:352-457 (:39-131, :235-257).
+ * num_splits > 1 uses `workspace` (mi_paged_decode_workspace_bytes) and a
+ * combine kernel; num_splits == 0 picks mi_paged_decode_default_splits.
+ * Query and out are contiguous [num_seqs, num_q_heads, head_dim].
+ */
+MI_API int mi_paged_decode(void *out, const void *query, const void *key_cache,
+                    const void *value_cache, int64_t num_blocks,
+                    int32_t block_size, int32_t num_q_heads,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                    const int32_t *block_tables, int64_t block_table_stride,
+                    const int32_t *context_lens, int64_t num_seqs, float scale,
+                    int32_t num_splits, void *workspace,
+                    size_t workspace_bytes, int32_t *dev_status, void *stream);
+
+/*
+ * Paged chunked-prefill attention (also mixed prefill + decode batches): the
+ * q_len = cu_seqlens_q[s+1]-cu_seqlens_q[s] query rows of sequence s sit at
+ * absolute positions prefix+i, prefix = context - q_len, context =
+ * cu_seqlens_k[s+1]-cu_seqlens_k[s]; row i attends causally to cached keys
+ * 0..prefix+i.  Replaces triton_paged_prefill + _paged_prefill_kernel,
+ * microinfer/layer/triton_paged_attention.py:260-339 (:133-233), and the
+ * torch reference _paged_attention_reference, paged_attention.py:22-67.
+ * `max_seqlen_q` bounds the per-sequence tile count (static launch shape).
+ */
+MI_API int mi_paged_prefill(void *out, const void *query, const void *key_cache,
+                     const void *value_cache, int64_t num_blocks,
+                     int32_t block_size, int32_t num_q_heads,
+                     int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                     const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k,
+                     const int32_t *block_tables, int64_t block_table_stride,
+                     int64_t num_seqs, int64_t num_tokens, int32_t max_seqlen_q,
+                     float scale, int32_t *dev_status, void *stream);
+
+/*
+ * Dense varlen causal prefill on this step's contiguous K/V (no cached
+ * prefix): keys/values [num_kv_tokens, num_kv_heads, head_dim] with row
+ * stride `kv_token_stride` (elements), cu_seqlens_q == cu_seqlens_k in the
+ * reference's use; K/V rows at or past `num_kv_tokens` are never read.
+ * Replaces _direct_prefill_flash / _direct_prefill_sdpa,
+ * microinfer/layer/cached_attention.py:17-55 (called at :87-101).
+ */
+MI_API int mi_varlen_prefill(void *out, const void *query, const void *keys,
+                      const void *values, int64_t kv_token_stride,
+                      int32_t num_q_heads, int32_t num_kv_heads,
+                      int32_t head_dim, int32_t dtype,
+                      const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k,
+                      int64_t num_seqs, int64_t num_tokens,
+                      int64_t num_kv_tokens, int32_t max_seqlen_q, float scale,
+                      int32_t *dev_status, void *stream);
+
+/*
+ * Block-table gather: out_keys[cu_seqlens_k[s] + t] = key_cache row of
+ * logical position t of sequence s, for t < context_s (same for values), in
+ * request-major order.  Replaces _gather_paged_kv,
+ * microinfer/layer/paged_attention.py:76-101 (test twin
+ * tests/support/kv.py:8-24).  `max_context` bounds the launch shape.
+ */
+MI_API int mi_gather_paged_kv(void *out_keys, void *out_values, const void *key_cache,
+                       const void *value_cache, int64_t num_blocks,
+                       int32_t block_size, int32_t num_kv_heads,
+                       int32_t head_dim, int32_t dtype,
+                       const int32_t *block_tables, int64_t block_table_stride,
+                       const int32_t *cu_seqlens_k, int64_t num_seqs,
+                       int32_t max_context, int32_t *dev_status, void *stream);
+
+/*
+ * Device-side copy-on-write of KV pages: for each pair p, copy block
+ * pairs[2p] -> pairs[2p+1] in every layer of a whole pool, for K and V.
+ * Pools are [num_layers, num_blocks, block_size, num_kv_heads, head_dim];
+ * `layer_stride_bytes` is the distance between layers and `block_bytes` the
+ * size of one block (block_size * num_kv_heads * head_dim * elem).  No
+ * destination may also be a source and destinations must be unique; ids
+ * outside the pool are skipped and flagged with MI_DEV_BAD_BLOCK.  The
+ * reference has no copy-on-write (prefix sharing only, never of a partial
+ * block: microinfer/engine/blockmanager.py:144-201); this entry point is
+ * what lets a sequence write into a private copy of a shared block.
+ */
+MI_API int mi_copy_blocks(void *key_pool, void *value_pool, int32_t num_layers,
+                   int64_t layer_stride_bytes, int64_t num_blocks,
+                   int64_t block_bytes, const int32_t *pairs,
+                   int64_t num_pairs, int32_t *dev_status, void *stream);
+
+/*
+ * Bounded-wait self test: one thread spins on `flag` (device int32) until it
+ * becomes non-zero or `timeout_ns` passes, then ORs MI_DEV_TIMEOUT into
+ * dev_status if it ran out.  Exercises the same bounded-wait helper every
+ * pipelined kernel uses, so timeouts can be tested without hanging a GPU.
+ */
+MI_API int mi_wait_flag_selftest(const int32_t *flag, int64_t timeout_ns,
+                          int32_t *dev_status, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MICROINFER_B200_H */

@@ -1,0 +1,49 @@
+"""B200-native (sm_100a) paged KV-cache hot path for the MicroInfer engine.
+
+A C-ABI shared library (``libmicroinfer_b200.so``, see include/microinfer_b200.h)
+holds the CUDA kernels; this package is the thin host layer that mirrors the
+reference's attention-backend interface:
+
+* ``worker.kv_store.store_kv`` / ``store_kv_slots``  - store_kvcache
+* ``layer.paged_attention.paged_decode``             - split-K paged decode
+* ``layer.paged_attention.paged_prefill``            - paged chunked prefill
+* ``layer.paged_attention.varlen_prefill``           - dense (no-prefix) prefill
+* ``layer.paged_attention.gather_paged_kv``          - block-table gather
+* ``worker.kv_cache.copy_blocks``                    - copy-on-write of pages
+* ``layer.paged_attention.paged_attention_meta``     - backend dispatch
+
+``install()`` rebinds a live ``microinfer`` import onto these entry points.
+"""
+
+from microinfer_b200._lib import check_device_status, load, read_device_status
+from microinfer_b200.install import install
+from microinfer_b200.layer.metadata import AttentionMetadata
+from microinfer_b200.layer.paged_attention import (
+    gather_paged_kv,
+    paged_attention_meta,
+    paged_decode,
+    paged_prefill,
+    select_split_k,
+    varlen_prefill,
+)
+from microinfer_b200.worker.kv_cache import KVCache, LayerKVCache, copy_blocks
+from microinfer_b200.worker.kv_store import store_kv, store_kv_slots
+
+__all__ = [
+    "AttentionMetadata",
+    "KVCache",
+    "LayerKVCache",
+    "check_device_status",
+    "copy_blocks",
+    "gather_paged_kv",
+    "install",
+    "load",
+    "paged_attention_meta",
+    "paged_decode",
+    "paged_prefill",
+    "read_device_status",
+    "select_split_k",
+    "store_kv",
+    "store_kv_slots",
+    "varlen_prefill",
+]

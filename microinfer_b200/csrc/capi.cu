@@ -1,0 +1,444 @@
+// extern "C" entry points of libmicroinfer_b200.so: argument validation,
+// kernel selection and launch.  Nothing here allocates or synchronises.
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "launch.cuh"
+#include "params.cuh"
+
+namespace mi {
+
+cudaError_t launch_store_kv(const StoreParams &p, int index_dtype, bool slots, int elem_bytes,
+                            bool vec16, cudaStream_t stream);
+cudaError_t launch_gather(const GatherParams &p, int64_t num_seqs, int32_t max_context, bool vec16,
+                          cudaStream_t stream);
+cudaError_t launch_cow(const CowParams &p, int32_t num_layers, int64_t num_pairs, bool vec16,
+                       cudaStream_t stream);
+cudaError_t launch_wait_flag(const int32_t *flag, int64_t timeout_ns, int32_t *status,
+                             cudaStream_t stream);
+cudaError_t launch_attn_generic(const AttnParams &p, int dtype, bool paged, cudaStream_t stream);
+bool decode_fast_supported(int dtype, int D, int G);
+cudaError_t launch_decode_fast(const DecodeParams &p, int dtype, int D, int G, int64_t num_seqs,
+                               int nsplit, cudaStream_t stream);
+bool prefill_tc_supported(int dtype, int D, int G, int block_size);
+cudaError_t launch_prefill_tc(const AttnParams &p, int dtype, int G, int32_t max_seqlen_q,
+                              bool paged, cudaStream_t stream);
+
+static int sm_counts[64];
+static std::once_flag sm_once[64];
+
+int sm_count_of(int device) {
+  if (device < 0 || device >= 64) return 148;
+  std::call_once(sm_once[device], [device] {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+      n = 148;
+    sm_counts[device] = n;
+  });
+  return sm_counts[device];
+}
+
+int sm_count_current() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  return sm_count_of(dev);
+}
+
+bool pdl_enabled() {
+  static const bool enabled = [] {
+    const char *v = std::getenv("MICROINFER_B200_PDL");
+    return !(v != nullptr && std::strcmp(v, "0") == 0);
+  }();
+  return enabled;
+}
+
+}  // namespace mi
+
+using namespace mi;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string &msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return MI_OK;
+  g_last_error = std::string("CUDA launch failed: ") + cudaGetErrorString(e);
+  return static_cast<int>(e);
+}
+
+int elem_size(int32_t dtype) {
+  switch (dtype) {
+    case MI_DTYPE_FLOAT32: return 4;
+    case MI_DTYPE_FLOAT16: return 2;
+    case MI_DTYPE_BFLOAT16: return 2;
+  }
+  return 0;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// This library carries its own (static) CUDA runtime, whose current device
+// is independent of the caller's.  Make the device that owns `p` current
+// before launching; a pointer that is not device memory is rejected here
+// instead of faulting inside a kernel.
+int select_device(const void *p) {
+  cudaPointerAttributes attr;
+  if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(MI_ERR_INVALID, "pointer is not known to the CUDA driver");
+  }
+  if (attr.type != cudaMemoryTypeDevice && attr.type != cudaMemoryTypeManaged)
+    return fail(MI_ERR_INVALID, "expected device memory, got a host pointer");
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || cur != attr.device) {
+    const cudaError_t e = cudaSetDevice(attr.device);
+    if (e != cudaSuccess) return fail(static_cast<int>(e), "cudaSetDevice failed");
+  }
+  return MI_OK;
+}
+
+constexpr float kLog2eHost = 1.4426950408889634f;
+
+}  // namespace
+
+extern "C" {
+
+int mi_abi_version(void) { return MI_ABI_VERSION; }
+
+const char *mi_last_error(void) { return g_last_error.c_str(); }
+
+int mi_device_sm_count(int device) {
+  int count = 0;
+  if (device < 0) return fail(MI_ERR_INVALID, "device must be >= 0");
+  if (cudaGetDeviceCount(&count) != cudaSuccess || device >= count)
+    return fail(MI_ERR_INVALID, "no such CUDA device");
+  return sm_count_of(device);
+}
+
+static int store_common(void *key_cache, void *value_cache, int64_t num_blocks, int32_t block_size,
+                        int32_t num_kv_heads, int32_t head_dim, int32_t dtype, const void *idx0,
+                        const void *idx1, int32_t index_dtype, const void *keys, const void *values,
+                        int64_t key_token_stride, int64_t value_token_stride, int64_t num_tokens,
+                        int32_t *dev_status, void *stream, bool slots) {
+  const int e = elem_size(dtype);
+  if (e == 0) return fail(MI_ERR_INVALID, "unknown dtype");
+  if (index_dtype != MI_INDEX_INT32 && index_dtype != MI_INDEX_INT64)
+    return fail(MI_ERR_INVALID, "index dtype must be int32 or int64");
+  if (num_tokens < 0) return fail(MI_ERR_INVALID, "num_tokens must be >= 0");
+  if (num_blocks <= 0 || block_size <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return fail(MI_ERR_INVALID, "cache dimensions must be positive");
+  if (key_token_stride < 0 || value_token_stride < 0)
+    return fail(MI_ERR_INVALID, "token strides must be >= 0");
+  if (num_tokens == 0) return MI_OK;
+  if (!key_cache || !value_cache || !keys || !values || !idx0 || (!slots && !idx1))
+    return fail(MI_ERR_INVALID, "null pointer");
+  if (const int s = select_device(key_cache)) return s;
+  const int64_t row_bytes = static_cast<int64_t>(num_kv_heads) * head_dim * e;
+  if (row_bytes > (1 << 30)) return fail(MI_ERR_INVALID, "token row too large");
+  StoreParams p;
+  p.key_cache = static_cast<char *>(key_cache);
+  p.value_cache = static_cast<char *>(value_cache);
+  p.keys = static_cast<const char *>(keys);
+  p.values = static_cast<const char *>(values);
+  p.idx0 = idx0;
+  p.idx1 = idx1;
+  p.num_blocks = num_blocks;
+  p.num_tokens = num_tokens;
+  p.key_stride_bytes = key_token_stride * e;
+  p.value_stride_bytes = value_token_stride * e;
+  p.block_size = block_size;
+  p.row_bytes = static_cast<int32_t>(row_bytes);
+  p.status = dev_status;
+  const bool vec16 = (row_bytes % 16 == 0) && aligned16(key_cache) && aligned16(value_cache) &&
+                     aligned16(keys) && aligned16(values) && (p.key_stride_bytes % 16 == 0) &&
+                     (p.value_stride_bytes % 16 == 0);
+  return cuda_status(
+      launch_store_kv(p, index_dtype, slots, e, vec16, static_cast<cudaStream_t>(stream)));
+}
+
+int mi_store_kv(void *key_cache, void *value_cache, int64_t num_blocks, int32_t block_size,
+                int32_t num_kv_heads, int32_t head_dim, int32_t dtype, const void *blocks,
+                const void *offsets, int32_t index_dtype, const void *keys, const void *values,
+                int64_t key_token_stride, int64_t value_token_stride, int64_t num_tokens,
+                int32_t *dev_status, void *stream) {
+  return store_common(key_cache, value_cache, num_blocks, block_size, num_kv_heads, head_dim, dtype,
+                      blocks, offsets, index_dtype, keys, values, key_token_stride,
+                      value_token_stride, num_tokens, dev_status, stream, false);
+}
+
+int mi_store_kv_slots(void *key_cache, void *value_cache, int64_t num_blocks, int32_t block_size,
+                      int32_t num_kv_heads, int32_t head_dim, int32_t dtype, const void *slots,
+                      int32_t index_dtype, const void *keys, const void *values,
+                      int64_t key_token_stride, int64_t value_token_stride, int64_t num_tokens,
+                      int32_t *dev_status, void *stream) {
+  return store_common(key_cache, value_cache, num_blocks, block_size, num_kv_heads, head_dim, dtype,
+                      slots, nullptr, index_dtype, keys, values, key_token_stride,
+                      value_token_stride, num_tokens, dev_status, stream, true);
+}
+
+size_t mi_paged_decode_workspace_bytes(int64_t num_seqs, int32_t num_q_heads, int32_t head_dim,
+                                       int32_t num_splits) {
+  if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || num_splits <= 1) return 0;
+  const size_t states = static_cast<size_t>(num_seqs) * num_q_heads * num_splits;
+  return states * (static_cast<size_t>(head_dim) + 2) * sizeof(float);
+}
+
+int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads, int32_t max_context_hint,
+                                   int device) {
+  if (num_seqs <= 0 || num_kv_heads <= 0) return 1;
+  const int64_t sms = sm_count_of(device < 0 ? 0 : device);
+  const int64_t base = num_seqs * num_kv_heads;
+  int64_t s = (2 * sms + base - 1) / base;
+  if (max_context_hint > 0) {
+    const int64_t chunks = (static_cast<int64_t>(max_context_hint) + 15) / 16;
+    const int64_t cap = chunks / 8;  // keep >= 2 chunks per warp (4 warps)
+    if (s > cap) s = cap;
+  }
+  if (s < 1) s = 1;
+  if (s > 256) s = 256;
+  return static_cast<int>(s);
+}
+
+int mi_paged_decode(void *out, const void *query, const void *key_cache, const void *value_cache,
+                    int64_t num_blocks, int32_t block_size, int32_t num_q_heads,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                    const int32_t *block_tables, int64_t block_table_stride,
+                    const int32_t *context_lens, int64_t num_seqs, float scale, int32_t num_splits,
+                    void *workspace, size_t workspace_bytes, int32_t *dev_status, void *stream) {
+  const int e = elem_size(dtype);
+  if (e == 0) return fail(MI_ERR_INVALID, "unknown dtype");
+  if (num_seqs < 0) return fail(MI_ERR_INVALID, "num_seqs must be >= 0");
+  if (num_blocks <= 0 || block_size <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return fail(MI_ERR_INVALID, "cache dimensions must be positive");
+  if (num_q_heads % num_kv_heads != 0)
+    return fail(MI_ERR_INVALID, "num_q_heads must be divisible by num_kv_heads");
+  if (head_dim > 256) return fail(MI_ERR_UNSUPPORTED, "head_dim > 256");
+  if (block_table_stride < 0) return fail(MI_ERR_INVALID, "block_table_stride must be >= 0");
+  if (num_splits < 0 || num_splits > 1024) return fail(MI_ERR_INVALID, "num_splits out of range");
+  if (num_seqs > 65535) return fail(MI_ERR_UNSUPPORTED, "more than 65535 sequences in one call");
+  if (num_seqs == 0) return MI_OK;
+  if (!out || !query || !key_cache || !value_cache || !block_tables || !context_lens)
+    return fail(MI_ERR_INVALID, "null pointer");
+  if (num_splits > 1 &&
+      (workspace == nullptr ||
+       workspace_bytes < mi_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, num_splits)))
+    return fail(MI_ERR_INVALID, "workspace too small for num_splits (see "
+                                "mi_paged_decode_workspace_bytes)");
+  if (const int s = select_device(key_cache)) return s;
+  const int G = num_q_heads / num_kv_heads;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool fast = decode_fast_supported(dtype, head_dim, G) && aligned16(key_cache) &&
+                    aligned16(value_cache) && aligned16(query);
+  if (!fast) {
+    AttnParams p = {};
+    p.out = out;
+    p.query = query;
+    p.key_base = static_cast<const char *>(key_cache);
+    p.value_base = static_cast<const char *>(value_cache);
+    p.block_tables = block_tables;
+    p.bt_stride = block_table_stride;
+    p.num_blocks = num_blocks;
+    p.block_size = block_size;
+    p.context_lens = context_lens;
+    p.num_seqs = num_seqs;
+    p.num_tokens = num_seqs;
+    p.num_q_heads = num_q_heads;
+    p.num_kv_heads = num_kv_heads;
+    p.head_dim = head_dim;
+    p.scale_log2 = scale * kLog2eHost;
+    p.status = dev_status;
+    return cuda_status(launch_attn_generic(p, dtype, true, st));
+  }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int nsplit = num_splits == 0 ? mi_paged_decode_default_splits(num_seqs, num_kv_heads, 0, dev)
+                               : num_splits;
+  DecodeParams p = {};
+  p.out = out;
+  p.query = query;
+  p.key_cache = static_cast<const char *>(key_cache);
+  p.value_cache = static_cast<const char *>(value_cache);
+  p.block_tables = block_tables;
+  p.context_lens = context_lens;
+  p.bt_stride = block_table_stride;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.scale_log2 = scale * kLog2eHost;
+  p.status = dev_status;
+  if (nsplit > 1) {
+    const size_t need = mi_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, nsplit);
+    if (workspace == nullptr || workspace_bytes < need)
+      return fail(MI_ERR_INVALID, "workspace too small for num_splits (see "
+                                  "mi_paged_decode_workspace_bytes)");
+    if ((reinterpret_cast<uintptr_t>(workspace) & 7u) != 0)
+      return fail(MI_ERR_ALIGNMENT, "workspace must be 8-byte aligned");
+    const size_t states = static_cast<size_t>(num_seqs) * num_q_heads * nsplit;
+    p.ws_acc = static_cast<float *>(workspace);
+    p.ws_ml = p.ws_acc + states * head_dim;
+  }
+  return cuda_status(launch_decode_fast(p, dtype, head_dim, G, num_seqs, nsplit, st));
+}
+
+static int prefill_common(void *out, const void *query, const void *kbase, const void *vbase,
+                          int64_t kv_token_stride, int64_t num_blocks, int32_t block_size,
+                          int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                          int32_t dtype, const int32_t *cu_q, const int32_t *cu_k,
+                          const int32_t *block_tables, int64_t bt_stride, int64_t num_seqs,
+                          int64_t num_tokens, int64_t num_kv_tokens, int32_t max_seqlen_q,
+                          float scale, int32_t *dev_status, void *stream, bool paged) {
+  const int e = elem_size(dtype);
+  if (e == 0) return fail(MI_ERR_INVALID, "unknown dtype");
+  if (num_seqs < 0 || num_tokens < 0) return fail(MI_ERR_INVALID, "negative sizes");
+  if (num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return fail(MI_ERR_INVALID, "head counts and head_dim must be positive");
+  if (num_q_heads % num_kv_heads != 0)
+    return fail(MI_ERR_INVALID, "num_q_heads must be divisible by num_kv_heads");
+  if (head_dim > 256) return fail(MI_ERR_UNSUPPORTED, "head_dim > 256");
+  if (paged && (num_blocks <= 0 || block_size <= 0 || bt_stride < 0))
+    return fail(MI_ERR_INVALID, "paged cache dimensions must be positive");
+  if (!paged && kv_token_stride < static_cast<int64_t>(num_kv_heads) * head_dim)
+    return fail(MI_ERR_INVALID, "kv_token_stride smaller than one K/V row");
+  if (num_tokens == 0 || num_seqs == 0) return MI_OK;
+  if (max_seqlen_q <= 0) return fail(MI_ERR_INVALID, "max_seqlen_q must be positive");
+  if (!out || !query || !kbase || !vbase || !cu_q || !cu_k || (paged && !block_tables))
+    return fail(MI_ERR_INVALID, "null pointer");
+  if (const int s = select_device(kbase)) return s;
+  AttnParams p = {};
+  p.out = out;
+  p.query = query;
+  p.key_base = static_cast<const char *>(kbase);
+  p.value_base = static_cast<const char *>(vbase);
+  p.kv_token_stride = kv_token_stride;
+  p.kv_rows = num_kv_tokens;
+  p.block_tables = block_tables;
+  p.bt_stride = bt_stride;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.cu_q = cu_q;
+  p.cu_k = cu_k;
+  p.num_seqs = num_seqs;
+  p.num_tokens = num_tokens;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.head_dim = head_dim;
+  p.scale_log2 = scale * kLog2eHost;
+  p.status = dev_status;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int G = num_q_heads / num_kv_heads;
+  const bool tc = prefill_tc_supported(dtype, head_dim, G, paged ? block_size : 16) &&
+                  aligned16(kbase) && aligned16(vbase) && aligned16(query) && aligned16(out) &&
+                  (paged || (kv_token_stride * e) % 16 == 0);
+  if (tc) return cuda_status(launch_prefill_tc(p, dtype, G, max_seqlen_q, paged, st));
+  return cuda_status(launch_attn_generic(p, dtype, paged, st));
+}
+
+int mi_paged_prefill(void *out, const void *query, const void *key_cache, const void *value_cache,
+                     int64_t num_blocks, int32_t block_size, int32_t num_q_heads,
+                     int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                     const int32_t *cu_seqlens_q, const int32_t *cu_seqlens_k,
+                     const int32_t *block_tables, int64_t block_table_stride, int64_t num_seqs,
+                     int64_t num_tokens, int32_t max_seqlen_q, float scale, int32_t *dev_status,
+                     void *stream) {
+  return prefill_common(out, query, key_cache, value_cache, 0, num_blocks, block_size, num_q_heads,
+                        num_kv_heads, head_dim, dtype, cu_seqlens_q, cu_seqlens_k, block_tables,
+                        block_table_stride, num_seqs, num_tokens, 0, max_seqlen_q, scale,
+                        dev_status, stream, true);
+}
+
+int mi_varlen_prefill(void *out, const void *query, const void *keys, const void *values,
+                      int64_t kv_token_stride, int32_t num_q_heads, int32_t num_kv_heads,
+                      int32_t head_dim, int32_t dtype, const int32_t *cu_seqlens_q,
+                      const int32_t *cu_seqlens_k, int64_t num_seqs, int64_t num_tokens,
+                      int64_t num_kv_tokens, int32_t max_seqlen_q, float scale,
+                      int32_t *dev_status, void *stream) {
+  if (num_kv_tokens < 0) return fail(MI_ERR_INVALID, "num_kv_tokens must be >= 0");
+  return prefill_common(out, query, keys, values, kv_token_stride, 0, 0, num_q_heads, num_kv_heads,
+                        head_dim, dtype, cu_seqlens_q, cu_seqlens_k, nullptr, 0, num_seqs,
+                        num_tokens, num_kv_tokens, max_seqlen_q, scale, dev_status, stream, false);
+}
+
+int mi_gather_paged_kv(void *out_keys, void *out_values, const void *key_cache,
+                       const void *value_cache, int64_t num_blocks, int32_t block_size,
+                       int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                       const int32_t *block_tables, int64_t block_table_stride,
+                       const int32_t *cu_seqlens_k, int64_t num_seqs, int32_t max_context,
+                       int32_t *dev_status, void *stream) {
+  const int e = elem_size(dtype);
+  if (e == 0) return fail(MI_ERR_INVALID, "unknown dtype");
+  if (num_blocks <= 0 || block_size <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return fail(MI_ERR_INVALID, "cache dimensions must be positive");
+  if (num_seqs < 0 || max_context < 0 || block_table_stride < 0)
+    return fail(MI_ERR_INVALID, "negative sizes");
+  if (num_seqs > 65535) return fail(MI_ERR_UNSUPPORTED, "more than 65535 sequences in one call");
+  if (num_seqs == 0 || max_context == 0) return MI_OK;
+  if (!out_keys || !out_values || !key_cache || !value_cache || !block_tables || !cu_seqlens_k)
+    return fail(MI_ERR_INVALID, "null pointer");
+  if (const int s = select_device(key_cache)) return s;
+  const int64_t row_bytes = static_cast<int64_t>(num_kv_heads) * head_dim * e;
+  GatherParams p;
+  p.out_keys = static_cast<char *>(out_keys);
+  p.out_values = static_cast<char *>(out_values);
+  p.key_cache = static_cast<const char *>(key_cache);
+  p.value_cache = static_cast<const char *>(value_cache);
+  p.block_tables = block_tables;
+  p.cu_seqlens_k = cu_seqlens_k;
+  p.block_table_stride = block_table_stride;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.row_bytes = static_cast<int32_t>(row_bytes);
+  // ~16 KB of rows per CTA per tensor.
+  int64_t rows = 16384 / row_bytes;
+  p.rows_per_cta = static_cast<int32_t>(rows < 1 ? 1 : rows);
+  p.status = dev_status;
+  const bool vec16 = row_bytes % 16 == 0 && aligned16(out_keys) && aligned16(out_values) &&
+                     aligned16(key_cache) && aligned16(value_cache);
+  return cuda_status(
+      launch_gather(p, num_seqs, max_context, vec16, static_cast<cudaStream_t>(stream)));
+}
+
+int mi_copy_blocks(void *key_pool, void *value_pool, int32_t num_layers, int64_t layer_stride_bytes,
+                   int64_t num_blocks, int64_t block_bytes, const int32_t *pairs, int64_t num_pairs,
+                   int32_t *dev_status, void *stream) {
+  if (num_layers <= 0 || num_blocks <= 0 || block_bytes <= 0)
+    return fail(MI_ERR_INVALID, "pool dimensions must be positive");
+  if (layer_stride_bytes < num_blocks * block_bytes)
+    return fail(MI_ERR_INVALID, "layer_stride_bytes smaller than one layer");
+  if (num_pairs < 0 || num_pairs > 2147483647) return fail(MI_ERR_INVALID, "num_pairs out of range");
+  if (num_layers > 65535) return fail(MI_ERR_UNSUPPORTED, "more than 65535 layers");
+  if (num_pairs == 0) return MI_OK;
+  if (!key_pool || !value_pool || !pairs) return fail(MI_ERR_INVALID, "null pointer");
+  if (const int s = select_device(key_pool)) return s;
+  CowParams p;
+  p.key_pool = static_cast<char *>(key_pool);
+  p.value_pool = static_cast<char *>(value_pool);
+  p.pairs = pairs;
+  p.layer_stride_bytes = layer_stride_bytes;
+  p.num_blocks = num_blocks;
+  p.block_bytes = block_bytes;
+  p.chunk_bytes = 8192;
+  p.status = dev_status;
+  const bool vec16 = aligned16(key_pool) && aligned16(value_pool) && block_bytes % 16 == 0 &&
+                     layer_stride_bytes % 16 == 0;
+  return cuda_status(launch_cow(p, num_layers, num_pairs, vec16, static_cast<cudaStream_t>(stream)));
+}
+
+int mi_wait_flag_selftest(const int32_t *flag, int64_t timeout_ns, int32_t *dev_status,
+                          void *stream) {
+  if (!flag || !dev_status) return fail(MI_ERR_INVALID, "null pointer");
+  if (timeout_ns <= 0 || timeout_ns > 10000000000ll)
+    return fail(MI_ERR_INVALID, "timeout_ns must be in (0, 10 s]");
+  if (const int s = select_device(flag)) return s;
+  return cuda_status(launch_wait_flag(flag, timeout_ns, dev_status, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

@@ -1,0 +1,34 @@
+// Host-side launch helpers: programmatic dependent launch (PDL) and cached
+// per-device SM counts.
+#pragma once
+
+#include <cuda_runtime.h>
+
+namespace mi {
+
+// SM count of the current device, cached per device id.
+int sm_count_current();
+int sm_count_of(int device);
+
+// Whether launches carry the programmatic-stream-serialization attribute.
+// Every kernel calls griddepcontrol.wait before touching upstream data, so
+// PDL only lets its launch and prologue overlap the previous kernel's tail.
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+}  // namespace mi

@@ -1,0 +1,87 @@
+// Kernel parameter blocks shared by the launchers and the C ABI layer.
+#pragma once
+
+#include <stdint.h>
+
+namespace mi {
+
+struct StoreParams {
+  char *key_cache;
+  char *value_cache;
+  const char *keys;
+  const char *values;
+  const void *idx0;
+  const void *idx1;
+  int64_t num_blocks;
+  int64_t num_tokens;
+  int64_t key_stride_bytes;
+  int64_t value_stride_bytes;
+  int32_t block_size;
+  int32_t row_bytes;
+  int32_t *status;
+};
+struct GatherParams {
+  char *out_keys;
+  char *out_values;
+  const char *key_cache;
+  const char *value_cache;
+  const int32_t *block_tables;
+  const int32_t *cu_seqlens_k;
+  int64_t block_table_stride;
+  int64_t num_blocks;
+  int32_t block_size;
+  int32_t row_bytes;
+  int32_t rows_per_cta;
+  int32_t *status;
+};
+struct CowParams {
+  char *key_pool;
+  char *value_pool;
+  const int32_t *pairs;
+  int64_t layer_stride_bytes;
+  int64_t num_blocks;
+  int64_t block_bytes;
+  int32_t chunk_bytes;
+  int32_t *status;
+};
+struct AttnParams {
+  void *out;
+  const void *query;
+  const char *key_base;
+  const char *value_base;
+  int64_t kv_token_stride;  // dense mode: elements between K/V token rows
+  int64_t kv_rows;          // dense mode: rows in keys/values (bounds check)
+  const int32_t *block_tables;
+  int64_t bt_stride;  // entries per block-table row; never read past
+  int64_t num_blocks;
+  int32_t block_size;
+  const int32_t *cu_q;
+  const int32_t *cu_k;
+  const int32_t *context_lens;
+  int64_t num_seqs;
+  int64_t num_tokens;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;
+  float scale_log2;
+  int32_t *status;
+};
+struct DecodeParams {
+  void *out;
+  const void *query;
+  const char *key_cache;
+  const char *value_cache;
+  const int32_t *block_tables;
+  const int32_t *context_lens;
+  float *ws_acc;
+  float *ws_ml;
+  int64_t bt_stride;
+  int64_t num_blocks;
+  int32_t block_size;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  float scale_log2;
+  int32_t *status;
+};
+
+}  // namespace mi

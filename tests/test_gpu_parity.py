@@ -1,0 +1,363 @@
+"""sm_100a kernels vs the reference (golden fixtures) and the CPU oracle.
+
+Every call goes through the package API, which calls the C ABI of
+libmicroinfer_b200.so.  Tolerances (from the spec): bit-exact for store,
+gather and copy-on-write; attention within 2e-2 abs / 1e-2 rel for fp16/bf16
+(fp32 accumulation) and 1e-5 for fp32.
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import microinfer_b200 as mi
+from microinfer_b200 import _lib
+from oracle import paged_oracle as po
+from tests.conftest import load_golden
+from tests.golden import cases
+
+pytestmark = pytest.mark.gpu
+
+TORCH = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+TOL = {"f32": (1e-5, 1e-5), "f16": (2e-2, 1e-2), "bf16": (2e-2, 1e-2)}
+
+
+def dev(a, dtype=None, device="cuda"):
+    a = np.ascontiguousarray(a)
+    if dtype == "bf16":
+        return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).to(device)
+    return torch.from_numpy(a).to(device)
+
+
+def host(t, dtype):
+    t = t.detach().contiguous().cpu()
+    if dtype == "bf16":
+        return t.view(torch.int16).numpy().view(np.uint16).copy()
+    return t.numpy().copy()
+
+
+def assert_close(actual, expected_bits, dtype):
+    atol, rtol = TOL[dtype]
+    np.testing.assert_allclose(po.to_f32(host(actual, dtype), dtype),
+                               po.to_f32(expected_bits, dtype), atol=atol, rtol=rtol)
+
+
+def _store(case, fast=False):
+    dt = case["dtype"]
+    kc, vc = dev(case["key_cache"], dt), dev(case["value_cache"], dt)
+    slots = dev(case["slots"])
+    k_new, v_new = dev(case["k_new"], dt), dev(case["v_new"], dt)
+    layer = mi.LayerKVCache(kc, vc)
+    if fast:
+        bs = case["block_size"]
+        sl = slots.long()
+        layer.write_fast(sl // bs, sl % bs, k_new, v_new)
+    else:
+        layer.write_checked(slots, k_new, v_new)
+    return layer
+
+
+@pytest.fixture(autouse=True)
+def _clean_status(cuda_device):
+    _lib.read_device_status(cuda_device)
+    yield
+    assert _lib.read_device_status(cuda_device) == 0, "a kernel flagged a bad id or timeout"
+
+
+PAGED = [c for c in cases.CASES if cases.kind(c) in ("decode", "prefill")]
+
+
+@pytest.mark.parametrize("name", PAGED)
+@pytest.mark.parametrize("fast", [False, True])
+def test_store_is_bit_exact(name, fast):
+    case = cases.build(name)
+    gold = load_golden(name)
+    layer = _store(case, fast=fast)
+    slots = case["slots"].astype(np.int64)
+    bs = case["block_size"]
+    dt = case["dtype"]
+    np.testing.assert_array_equal(host(layer.keys, dt)[slots // bs, slots % bs], gold["stored_k"])
+    np.testing.assert_array_equal(host(layer.values, dt)[slots // bs, slots % bs], gold["stored_v"])
+    # nothing else in the pool changed
+    untouched = np.ones(case["key_cache"].shape[:2], bool)
+    untouched[slots // bs, slots % bs] = False
+    np.testing.assert_array_equal(host(layer.keys, dt)[untouched], case["key_cache"][untouched])
+
+
+@pytest.mark.parametrize("name", PAGED)
+def test_attention_matches_reference_and_oracle(name):
+    case = cases.build(name)
+    gold = load_golden(name)
+    dt = case["dtype"]
+    layer = _store(case)
+    q = dev(case["query"], dt)
+    table = dev(case["block_tables"])
+    if case["kind"] == "decode":
+        out = mi.paged_decode(q, layer.keys, layer.values, table, dev(case["contexts"]),
+                              scale=case["scale"])
+        cu_q = np.arange(len(case["contexts"]) + 1)
+    else:
+        out = mi.paged_prefill(q, layer.keys, layer.values, dev(case["cu_seqlens_q"]),
+                               dev(case["cu_seqlens_k"]), table,
+                               max_seqlen_q=int(case["q_lens"].max()), scale=case["scale"])
+        cu_q = case["cu_seqlens_q"]
+    assert out.dtype == TORCH[dt] and out.shape == q.shape
+    assert torch.isfinite(out.float()).all()
+    assert_close(out, gold["out"], dt)
+    kc, vc = host(layer.keys, dt), host(layer.values, dt)
+    expected = po.paged_attention(case["query"], kc, vc, case["block_tables"], case["contexts"],
+                                  cu_q, scale=case["scale"], dtype=dt)
+    assert_close(out, expected, dt)
+
+
+@pytest.mark.parametrize("name", [c for c in PAGED if cases.kind(c) == "decode"])
+@pytest.mark.parametrize("split_k", [1, 2, 3, 7, 37])
+def test_decode_split_k_matches_reference(name, split_k):
+    case = cases.build(name)
+    gold = load_golden(name)
+    dt = case["dtype"]
+    layer = _store(case)
+    out = mi.paged_decode(dev(case["query"], dt), layer.keys, layer.values,
+                          dev(case["block_tables"]), dev(case["contexts"]), scale=case["scale"],
+                          split_k=split_k)
+    assert_close(out, gold["out"], dt)
+
+
+@pytest.mark.parametrize("name", ["cfg1_decode_f32", "cfg2_layer_bf16", "decode_bs64_bf16"])
+def test_decode_kernel_agrees_with_prefill_kernel(name):
+    """The decode kernels and the varlen prefill kernels are separate code."""
+    case = cases.build(name)
+    dt = case["dtype"]
+    layer = _store(case)
+    q, table, ctx = dev(case["query"], dt), dev(case["block_tables"]), dev(case["contexts"])
+    a = mi.paged_decode(q, layer.keys, layer.values, table, ctx, scale=case["scale"])
+    n = q.shape[0]
+    cu_q = torch.arange(n + 1, dtype=torch.int32, device="cuda")
+    cu_k = torch.zeros(n + 1, dtype=torch.int32, device="cuda")
+    cu_k[1:] = torch.cumsum(ctx, 0)
+    b = mi.paged_prefill(q, layer.keys, layer.values, cu_q, cu_k, table, max_seqlen_q=1,
+                         scale=case["scale"])
+    atol, rtol = TOL[dt]
+    torch.testing.assert_close(a.float(), b.float(), atol=atol, rtol=rtol)
+
+
+@pytest.mark.parametrize("name", PAGED)
+def test_gather_is_bit_exact(name):
+    case = cases.build(name)
+    gold = load_golden(name)
+    dt = case["dtype"]
+    layer = _store(case)
+    keys, values = mi.gather_paged_kv(layer.keys, layer.values, dev(case["block_tables"]),
+                                      case["contexts"].tolist(), case["block_size"])
+    assert keys.shape[0] == int(gold["gather_rows"])
+    assert cases.digest(host(keys, dt)) == str(gold["gather_k_digest"])
+    assert cases.digest(host(values, dt)) == str(gold["gather_v_digest"])
+
+
+@pytest.mark.parametrize("name", ["direct_bf16", "direct_f32"])
+def test_direct_prefill_matches_reference(name):
+    case = cases.build(name)
+    gold = load_golden(name)
+    dt = case["dtype"]
+    cu = dev(case["cu_seqlens"])
+    lengths = np.diff(case["cu_seqlens"])
+    out = mi.varlen_prefill(dev(case["query"], dt), dev(case["keys"], dt), dev(case["values"], dt),
+                            cu, cu, max_seqlen_q=int(lengths.max()), scale=case["scale"])
+    assert_close(out, gold["out"], dt)
+
+
+def test_copy_on_write_is_bit_exact():
+    case = cases.build("cow_bf16")
+    gold = load_golden("cow_bf16")
+    kp, vp = dev(case["key_pool"], "bf16"), dev(case["value_pool"], "bf16")
+    mi.copy_blocks(kp, vp, torch.from_numpy(case["pairs"]))
+    assert cases.digest(host(kp, "bf16")) == str(gold["key_pool_digest"])
+    assert cases.digest(host(vp, "bf16")) == str(gold["value_pool_digest"])
+
+
+def test_write_checked_padding_matches_reference():
+    case = cases.build("write_checked_f32")
+    gold = load_golden("write_checked_f32")
+    layer = mi.LayerKVCache(dev(case["key_cache"]), dev(case["value_cache"]))
+    layer.write_checked(dev(case["slots"]), dev(case["keys"]), dev(case["values"]))
+    np.testing.assert_array_equal(host(layer.keys, "f32"), gold["key_cache"])
+    np.testing.assert_array_equal(host(layer.values, "f32"), gold["value_cache"])
+
+
+@pytest.mark.parametrize("slots", [[0, 8], [0, -2], [0, 0]])
+def test_invalid_writes_are_atomic_on_device(slots, cuda_device):
+    layer = mi.LayerKVCache(torch.full((2, 4, 1, 2), 7.0, device="cuda"),
+                            torch.full((2, 4, 1, 2), 7.0, device="cuda"))
+    with pytest.raises(ValueError):
+        layer.write_checked(torch.tensor(slots, device="cuda"), torch.zeros(2, 1, 2, device="cuda"),
+                            torch.zeros(2, 1, 2, device="cuda"))
+    assert (layer.keys == 7).all() and (layer.values == 7).all()
+
+
+# --- known answers of the reference tests, on the device ---------------------
+
+def test_kat_isolation_and_padding():
+    q = torch.zeros(2, 1, 2, device="cuda")
+    k = torch.zeros(3, 2, 1, 2, device="cuda")
+    v = torch.full_like(k, 999)
+    v[2, 0], v[2, 1], v[0, 0] = 2, 4, 10
+    table = torch.tensor([[2, -1], [0, -1]], device="cuda")
+    out = mi.paged_decode(q, k, v, table, torch.tensor([2, 1], device="cuda"))
+    torch.testing.assert_close(out.cpu(), torch.tensor([[[3.0, 3.0]], [[10.0, 10.0]]]))
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_kat_large_logits(dtype):
+    query = torch.full((1, 2, 4), 1000.0, dtype=dtype, device="cuda")
+    keys = torch.full((1, 2, 1, 4), 1000.0, dtype=dtype, device="cuda")
+    values = torch.tensor([2.0, 4.0], dtype=dtype, device="cuda").reshape(1, 2, 1, 1).expand_as(
+        keys).contiguous()
+    table = torch.tensor([[0]], device="cuda")
+    out = mi.paged_decode(query, keys, values, table, torch.tensor([2], device="cuda"))
+    torch.testing.assert_close(out, torch.full_like(query, 3.0))
+    meta = mi.AttentionMetadata.build(is_prefill=True, cu_seqlens_q=torch.tensor([0, 1], device="cuda"),
+                                      cu_seqlens_k=torch.tensor([0, 2], device="cuda"),
+                                      max_seqlen_q=1, block_tables=table)
+    torch.testing.assert_close(mi.paged_attention_meta(query, keys, values, meta),
+                               torch.full_like(query, 3.0))
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("prefix,q_len", [(0, 3), (2, 1), (1, 2)])
+def test_tiny_paged_causal_gqa(dtype, prefix, q_len):
+    """tests/components/test_paged_attention.py:10-46 shape: D=4, bs=2, blocks [2, 0]."""
+    rng = np.random.default_rng(prefix * 10 + q_len)
+    ctx = prefix + q_len
+    q = po.from_f32(rng.standard_normal((q_len, 4, 4), dtype=np.float32), dtype)
+    kc = po.from_f32(np.full((3, 2, 2, 4), 1000.0, np.float32), dtype)
+    vc = po.from_f32(np.full((3, 2, 2, 4), -1000.0, np.float32), dtype)
+    table = [2, 0]
+    for pos in range(ctx):
+        kc[table[pos // 2], pos % 2] = po.from_f32(rng.standard_normal((2, 4), dtype=np.float32), dtype)
+        vc[table[pos // 2], pos % 2] = po.from_f32(rng.standard_normal((2, 4), dtype=np.float32), dtype)
+    expected = po.paged_attention(q, kc, vc, np.array([table]), [ctx], [0, q_len], scale=0.5,
+                                  dtype=dtype)
+    meta = mi.AttentionMetadata.build(
+        is_prefill=q_len > 1 or prefix == 0,
+        cu_seqlens_q=torch.tensor([0, q_len], device="cuda"),
+        cu_seqlens_k=torch.tensor([0, ctx], device="cuda"),
+        max_seqlen_q=q_len, context_lens=torch.tensor([ctx], device="cuda"),
+        block_tables=torch.tensor([table], device="cuda"))
+    out = mi.paged_attention_meta(dev(q, dtype), dev(kc, dtype), dev(vc, dtype), meta, scale=0.5)
+    assert_close(out, expected, dtype)
+
+
+# --- full-size properties ------------------------------------------------------
+
+def test_config2_full_28_layers_split_invariance_and_roundtrip():
+    """BASELINE config 2 at full size: 28 layers x 1024 blocks, N=8, ctx U[128,512]."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    layers, nb, bs, hkv, hq, d, n = 28, 1024, 16, 8, 16, 128, 8
+    pool = mi.KVCache(layers, nb, bs, hkv, d, dtype=torch.bfloat16, device="cuda")
+    pool.keys.normal_(generator=g).mul_(0.5)
+    pool.values.normal_(generator=g).mul_(0.5)
+    ctx = torch.randint(128, 513, (n,), generator=g, device="cuda", dtype=torch.int32)
+    need = ((ctx + bs - 1) // bs).tolist()
+    perm = torch.randperm(nb, generator=g, device="cuda").to(torch.int32)
+    table = torch.full((n, max(need)), -1, dtype=torch.int32, device="cuda")
+    at = 0
+    for r, k in enumerate(need):
+        table[r, :k] = perm[at:at + k]
+        at += k
+    pos = (ctx - 1).long()
+    slots = (table[torch.arange(n, device="cuda"), pos // bs].long() * bs + pos % bs).to(torch.int32)
+    q = torch.randn(layers, n, hq, d, generator=g, device="cuda").to(torch.bfloat16)
+    kn = torch.randn(layers, n, hkv, d, generator=g, device="cuda").to(torch.bfloat16)
+    vn = torch.randn(layers, n, hkv, d, generator=g, device="cuda").to(torch.bfloat16)
+    outs = {}
+    for split in (1, 5, 16):
+        res = []
+        for layer in range(layers):
+            view = pool.layer(layer)
+            view.write_slots(slots, kn[layer], vn[layer])
+            res.append(mi.paged_decode(q[layer], view.keys, view.values, table, ctx, split_k=split))
+        outs[split] = torch.stack(res).float()
+    torch.testing.assert_close(outs[5], outs[1], atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(outs[16], outs[1], atol=2e-2, rtol=1e-2)
+    # store -> gather round trip: the gathered last row of each sequence is the stored token
+    view = pool.layer(layers - 1)
+    keys, values = mi.gather_paged_kv(view.keys, view.values, table, ctx.tolist(), bs)
+    ends = torch.cumsum(ctx.long(), 0) - 1
+    assert torch.equal(keys[ends], kn[-1]) and torch.equal(values[ends], vn[-1])
+    # spot-check one layer against the oracle
+    dt = "bf16"
+    expected = po.paged_decode(host(q[0], dt), host(pool.keys[0], dt), host(pool.values[0], dt),
+                               table.cpu().numpy(), ctx.cpu().numpy(), scale=1 / math.sqrt(d),
+                               dtype=dt)
+    assert_close(outs[1][0].to(torch.bfloat16), expected, dt)
+
+
+def test_decode_is_cuda_graph_capturable():
+    case = cases.build("cfg2_layer_bf16")
+    dt = case["dtype"]
+    layer = _store(case)
+    q = dev(case["query"], dt)
+    table = dev(case["block_tables"])
+    ctx = dev(case["contexts"])
+    split = mi.select_split_k(q.shape[0], 8, q.device)
+    eager = mi.paged_decode(q, layer.keys, layer.values, table, ctx, split_k=split)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        mi.paged_decode(q, layer.keys, layer.values, table, ctx, split_k=split)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = mi.paged_decode(q, layer.keys, layer.values, table, ctx, split_k=split)
+    graph.replay()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out, eager)
+    # replay with shorter contexts: the graph reads context_lens from the device
+    ctx.sub_(7)
+    expected = mi.paged_decode(q, layer.keys, layer.values, table, ctx, split_k=split)
+    graph.replay()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out, expected)
+
+
+# --- device status: bad ids are flagged and skipped, never dereferenced -------
+
+def test_bad_block_id_is_flagged_not_dereferenced(cuda_device):
+    kc = torch.randn(4, 16, 8, 128, device="cuda").to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    q = torch.randn(1, 16, 128, device="cuda").to(torch.bfloat16)
+    table = torch.tensor([[0, 1_000_000]], dtype=torch.int32, device="cuda")
+    mi.paged_decode(q, kc, vc, table, torch.tensor([20], device="cuda"), split_k=1)
+    assert _lib.read_device_status(cuda_device) & _lib.DEV_BAD_BLOCK
+    # context longer than the table row: read stops at the row's end
+    table = torch.tensor([[0, 1]], dtype=torch.int32, device="cuda")
+    mi.paged_decode(q, kc, vc, table, torch.tensor([40], device="cuda"), split_k=2)
+    assert _lib.read_device_status(cuda_device) & _lib.DEV_BAD_BLOCK
+    with pytest.raises(RuntimeError):
+        mi.paged_decode(q, kc, vc, table, torch.tensor([40], device="cuda"), split_k=1)
+        mi.check_device_status(cuda_device)
+
+
+def test_bad_slot_is_flagged_not_written(cuda_device):
+    kc = torch.zeros(2, 4, 1, 8, device="cuda")
+    vc = torch.zeros_like(kc)
+    mi.store_kv_slots(kc, vc, torch.tensor([3, 99], dtype=torch.int32, device="cuda"),
+                      torch.ones(2, 1, 8, device="cuda"), torch.ones(2, 1, 8, device="cuda"))
+    assert _lib.read_device_status(cuda_device) & _lib.DEV_BAD_SLOT
+    assert kc.sum().item() == 8 and vc.sum().item() == 8
+
+
+def test_bounded_wait_times_out_and_context_survives(cuda_device):
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    status = _lib.status_buffer(cuda_device)
+    _lib.call("mi_wait_flag_selftest", flag.data_ptr(), 200_000_000, status.data_ptr(),
+              _lib.stream_of(cuda_device))
+    assert _lib.read_device_status(cuda_device) & _lib.DEV_TIMEOUT
+    # flag already set: returns at once, no timeout
+    flag.fill_(1)
+    _lib.call("mi_wait_flag_selftest", flag.data_ptr(), 200_000_000, status.data_ptr(),
+              _lib.stream_of(cuda_device))
+    assert _lib.read_device_status(cuda_device) == 0
+    assert (torch.ones(4, device="cuda") * 2).sum().item() == 8
