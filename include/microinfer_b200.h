@@ -179,7 +179,8 @@ MI_API int mi_varlen_prefill(void *out, const void *query, const void *keys,
  * logical position t of sequence s, for t < context_s (same for values), in
  * request-major order.  Replaces _gather_paged_kv,
  * microinfer/layer/paged_attention.py:76-101 (test twin
- * tests/support/kv.py:8-24).  `max_context` bounds the launch shape.
+ * tests/support/kv.py:8-24).  `max_context` bounds the launch shape;
+ * `out_rows` is the row capacity of out_keys/out_values (never written past).
  */
 MI_API int mi_gather_paged_kv(void *out_keys, void *out_values, const void *key_cache,
                        const void *value_cache, int64_t num_blocks,
@@ -187,7 +188,8 @@ MI_API int mi_gather_paged_kv(void *out_keys, void *out_values, const void *key_
                        int32_t head_dim, int32_t dtype,
                        const int32_t *block_tables, int64_t block_table_stride,
                        const int32_t *cu_seqlens_k, int64_t num_seqs,
-                       int32_t max_context, int32_t *dev_status, void *stream);
+                       int64_t out_rows, int32_t max_context,
+                       int32_t *dev_status, void *stream);
 
 /*
  * Device-side copy-on-write of KV pages: for each pair p, copy block

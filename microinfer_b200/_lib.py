@@ -61,7 +61,7 @@ SIGNATURES = {
     ),
     "mi_gather_paged_kv": (
         ctypes.c_int,
-        [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _I32, _P, _P],
+        [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _I64, _I32, _P, _P],
     ),
     "mi_copy_blocks": (ctypes.c_int, [_P, _P, _I32, _I64, _I64, _I64, _P, _I64, _P, _P]),
     "mi_wait_flag_selftest": (ctypes.c_int, [_P, _I64, _P, _P]),

@@ -64,7 +64,11 @@ __global__ void __launch_bounds__(128) attn_generic_kernel(AttnParams p) {
     ctx = p.context_lens[seq];
   }
   const int64_t pos = ctx - q_len + (t - q_start);  // absolute position of this query row
-  const int64_t nkeys = min(pos + 1, ctx);
+  int64_t nkeys = min(pos + 1, ctx);
+  if (PAGED && nkeys > p.bt_stride * p.block_size) {  // beyond what the table row addresses
+    if (lane == 0) flag_status(p.status, MI_DEV_BAD_BLOCK);
+    nkeys = p.bt_stride * p.block_size;
+  }
   const int kvh = h / (p.num_q_heads / p.num_kv_heads);
 
   const T *q = static_cast<const T *>(p.query) + (t * p.num_q_heads + h) * D;
@@ -234,7 +238,12 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
   __syncwarp();
 
   pdl_wait();
-  const int ctx = p.context_lens[seq];
+  int ctx = p.context_lens[seq];
+  const int64_t cap = p.bt_stride * p.block_size;  // keys the table row can address
+  if (ctx > cap) {
+    if (threadIdx.x == 0 && split == 0) flag_status(p.status, MI_DEV_BAD_BLOCK);
+    ctx = static_cast<int>(cap);
+  }
   const int nchunks = (ctx + C::kKeys - 1) / C::kKeys;
   const int cps = (nchunks + nsplit - 1) / nsplit;
   const int c_begin = split * cps;

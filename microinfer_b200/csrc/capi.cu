@@ -371,13 +371,13 @@ int mi_gather_paged_kv(void *out_keys, void *out_values, const void *key_cache,
                        const void *value_cache, int64_t num_blocks, int32_t block_size,
                        int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
                        const int32_t *block_tables, int64_t block_table_stride,
-                       const int32_t *cu_seqlens_k, int64_t num_seqs, int32_t max_context,
-                       int32_t *dev_status, void *stream) {
+                       const int32_t *cu_seqlens_k, int64_t num_seqs, int64_t out_rows,
+                       int32_t max_context, int32_t *dev_status, void *stream) {
   const int e = elem_size(dtype);
   if (e == 0) return fail(MI_ERR_INVALID, "unknown dtype");
   if (num_blocks <= 0 || block_size <= 0 || num_kv_heads <= 0 || head_dim <= 0)
     return fail(MI_ERR_INVALID, "cache dimensions must be positive");
-  if (num_seqs < 0 || max_context < 0 || block_table_stride < 0)
+  if (num_seqs < 0 || max_context < 0 || block_table_stride < 0 || out_rows < 0)
     return fail(MI_ERR_INVALID, "negative sizes");
   if (num_seqs > 65535) return fail(MI_ERR_UNSUPPORTED, "more than 65535 sequences in one call");
   if (num_seqs == 0 || max_context == 0) return MI_OK;
@@ -399,6 +399,7 @@ int mi_gather_paged_kv(void *out_keys, void *out_values, const void *key_cache,
   // ~16 KB of rows per CTA per tensor.
   int64_t rows = 16384 / row_bytes;
   p.rows_per_cta = static_cast<int32_t>(rows < 1 ? 1 : rows);
+  p.out_rows = out_rows;
   p.status = dev_status;
   const bool vec16 = row_bytes % 16 == 0 && aligned16(out_keys) && aligned16(out_values) &&
                      aligned16(key_cache) && aligned16(value_cache);

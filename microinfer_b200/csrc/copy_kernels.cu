@@ -135,6 +135,10 @@ __global__ void __launch_bounds__(256) gather_kernel(GatherParams p) {
     }
     const int64_t src_row = blk * p.block_size + pos % p.block_size;
     const int64_t dst_row = base + pos;
+    if (dst_row < 0 || dst_row >= p.out_rows) {
+      flag_status(p.status, MI_DEV_BAD_SLOT);
+      continue;
+    }
     if (VEC16) {
       const uint4 k = *reinterpret_cast<const uint4 *>(p.key_cache + src_row * p.row_bytes + e * 16);
       const uint4 v = *reinterpret_cast<const uint4 *>(p.value_cache + src_row * p.row_bytes + e * 16);

@@ -32,6 +32,7 @@ struct GatherParams {
   int32_t block_size;
   int32_t row_bytes;
   int32_t rows_per_cta;
+  int64_t out_rows;  // rows of out_keys/out_values; never written past
   int32_t *status;
 };
 struct CowParams {

@@ -228,7 +228,7 @@ def gather_paged_kv(key_cache, value_cache, block_tables, contexts, block_size,
         "mi_gather_paged_kv", keys.data_ptr(), values.data_ptr(), key_cache.data_ptr(),
         value_cache.data_ptr(), key_cache.shape[0], block_size, num_kv_heads, head_dim,
         _lib.dtype_code(key_cache.dtype), block_tables.data_ptr(), block_tables.stride(0),
-        cu_seqlens_k.data_ptr(), len(contexts), max(contexts),
+        cu_seqlens_k.data_ptr(), len(contexts), total, max(contexts),
         _lib.status_buffer(device).data_ptr(), _lib.stream_of(device),
     )
     return keys, values
