@@ -395,6 +395,40 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_profile(args):
+    """Small fixed case for ncu: config-2 shapes on 4 layer pools (256 MB > L2).
+
+    Eager launches (no graph), `--steps` iterations of store + decode per
+    layer, so an ncu capture with -k/-s/-c stays small and ends by itself.
+    """
+    import torch
+
+    import microinfer_b200 as mi
+
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    layers = 4
+    ctx, table, slots = make_batch(1000, device)
+    ctx_d, table_d, slots_d = ctx.to(device), table.to(device), slots.to(device)
+    pool = mi.KVCache(layers, NB, BS, HKV, D, dtype=torch.bfloat16, device=device)
+    g = torch.Generator(device=device).manual_seed(0)
+    pool.keys.normal_(generator=g).mul_(0.5)
+    pool.values.normal_(generator=g).mul_(0.5)
+    q = torch.randn(layers, NSEQ, HQ, D, generator=g, device=device).to(torch.bfloat16)
+    kn = torch.randn(layers, NSEQ, HKV, D, generator=g, device=device).to(torch.bfloat16)
+    split = args.split_k or mi.select_split_k(NSEQ, HKV, device)
+    for _ in range(args.steps):
+        for i in range(layers):
+            view = pool.layer(i)
+            view.write_slots(slots_d, kn[i], kn[i])
+            mi.paged_decode(q[i], view.keys, view.values, table_d, ctx_d, split_k=split)
+    torch.cuda.synchronize(device)
+    mi.check_device_status(device)
+    dec_b, _ = algorithmic_bytes(ctx.tolist())
+    print(json.dumps({"profile": args.profile, "layers": layers, "iterations": args.steps,
+                      "split_k": split, "decode_bytes_per_launch": dec_b}))
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -402,8 +436,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=["decode"], default=None,
+                    help="run a small eager case for ncu instead of the benchmark")
+    ap.add_argument("--split-k", type=int, default=0)
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.profile:
+        run_profile(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

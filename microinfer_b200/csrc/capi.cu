@@ -196,7 +196,9 @@ int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads, int32
   if (num_seqs <= 0 || num_kv_heads <= 0) return 1;
   const int64_t sms = sm_count_of(device < 0 ? 0 : device);
   const int64_t base = num_seqs * num_kv_heads;
-  int64_t s = (2 * sms + base - 1) / base;
+  // Two decode CTAs fit per SM; stay within that single wave (a second,
+  // partial wave doubles the latency of a short decode).
+  int64_t s = (2 * sms) / base;
   if (max_context_hint > 0) {
     const int64_t chunks = (static_cast<int64_t>(max_context_hint) + 15) / 16;
     const int64_t cap = chunks / 8;  // keep >= 2 chunks per warp (4 warps)

@@ -48,8 +48,8 @@ def test_workspace_and_split_policy():
     lib = _lib.load()
     assert lib.mi_paged_decode_workspace_bytes(8, 16, 128, 1) == 0
     assert lib.mi_paged_decode_workspace_bytes(8, 16, 128, 5) == 8 * 16 * 5 * 130 * 4
-    # 148 SMs assumed without a device: ceil(2*148 / (8*8)) = 5
-    assert lib.mi_paged_decode_default_splits(8, 8, 0, 0) == 5
+    # 148 SMs assumed without a device: floor(2*148 / (8*8)) = 4 (one wave)
+    assert lib.mi_paged_decode_default_splits(8, 8, 0, 0) == 4
     assert lib.mi_paged_decode_default_splits(256, 8, 0, 0) == 1
     assert lib.mi_paged_decode_default_splits(1, 8, 0, 0) == 37
     # a context hint caps splits at >= 2 chunks per warp
