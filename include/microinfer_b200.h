@@ -139,6 +139,30 @@ MI_API int mi_paged_decode(void *out, const void *query, const void *key_cache,
                     size_t workspace_bytes, int32_t *dev_status, void *stream);
 
 /*
+ * Allocation-free paged decode.  No counterpart in the reference: it exists
+ * for callers that cannot allocate device memory on the call path (a serving
+ * loop that reserved nearly all HBM for the KV pool up front, or an FFI host
+ * that owns only the buffers it was given).  Same arguments and results as
+ * mi_paged_decode without the workspace: split-K states go to a 2 MiB scratch
+ * array built into the library (held by every GPU that loads it until exit).
+ * Limit: num_seqs * num_q_heads * num_splits * (head_dim + 2) * 4 bytes must
+ * fit in 2 MiB, else MI_ERR_INVALID.  The first call on a device looks up the
+ * array's device address (make it outside stream capture).  Calls share the
+ * array, so calls that overlap on the GPU race; serialise them.  Calls no
+ * cudaMalloc/cudaFree.
+ */
+MI_API int mi_paged_decode_noalloc(void *out, const void *query,
+                            const void *key_cache, const void *value_cache,
+                            int64_t num_blocks, int32_t block_size,
+                            int32_t num_q_heads, int32_t num_kv_heads,
+                            int32_t head_dim, int32_t dtype,
+                            const int32_t *block_tables,
+                            int64_t block_table_stride,
+                            const int32_t *context_lens, int64_t num_seqs,
+                            float scale, int32_t num_splits,
+                            int32_t *dev_status, void *stream);
+
+/*
  * Paged chunked-prefill attention (also mixed prefill + decode batches): the
  * q_len = cu_seqlens_q[s+1]-cu_seqlens_q[s] query rows of sequence s sit at
  * absolute positions prefix+i, prefix = context - q_len, context =

@@ -49,6 +49,11 @@ SIGNATURES = {
         [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _F, _I32, _P,
          _SZ, _P, _P],
     ),
+    "mi_paged_decode_noalloc": (
+        ctypes.c_int,
+        [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _F, _I32, _P,
+         _P],
+    ),
     "mi_paged_prefill": (
         ctypes.c_int,
         [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _I64, _I64, _I64, _I32,

@@ -109,6 +109,13 @@ constexpr float kLog2eHost = 1.4426950408889634f;
 
 }  // namespace
 
+// Error reporting and device selection for entry points defined in other
+// translation units (their messages surface through mi_last_error()).
+namespace mi {
+int capi_fail(int code, const char *msg) { return fail(code, msg); }
+int capi_select_device(const void *p) { return select_device(p); }
+}  // namespace mi
+
 extern "C" {
 
 int mi_abi_version(void) { return MI_ABI_VERSION; }

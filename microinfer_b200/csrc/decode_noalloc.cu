@@ -1,0 +1,158 @@
+// Allocation-free split-K paged decode.
+//
+// Some callers cannot allocate device memory on the call path: a serving
+// loop that reserved nearly all of HBM for the KV pool up front and forbids
+// allocation afterwards, or a host runtime reaching this library through an
+// FFI that only owns the buffers it was handed and has no device allocator to
+// ask for a workspace.  mi_paged_decode_noalloc serves them: it runs the same
+// decode kernels as mi_paged_decode, but the split-K partial states live in a
+// fixed scratch array compiled into this library instead of a caller-provided
+// workspace.
+//
+// The scratch is a file-scope __device__ array of kNoAllocScratchBytes (2 MiB)
+// that every GPU loading the library holds until the process exits.  Host
+// code cannot use the array's name as a device address, so on the first call
+// on each device (with that device current) its address is looked up once
+// with cudaGetSymbolAddress and cached; make that first call outside any
+// stream capture.  All calls share the one array and it keeps the previous
+// call's contents: the kernels write every split state before the combine
+// reads it, so nothing needs clearing, but calls that overlap on the GPU (two
+// streams, or two threads) race on the array and must be serialised by the
+// caller.
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.cuh"
+#include "params.cuh"
+
+namespace mi {
+
+int capi_fail(int code, const char *msg);
+int capi_select_device(const void *p);
+bool decode_fast_supported(int dtype, int D, int G);
+cudaError_t launch_decode_fast(const DecodeParams &p, int dtype, int D, int G, int64_t num_seqs,
+                               int nsplit, cudaStream_t stream);
+cudaError_t launch_attn_generic(const AttnParams &p, int dtype, bool paged, cudaStream_t stream);
+
+constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;
+
+static __device__ __align__(256) float g_decode_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+float *g_scratch_ptr[kMaxDevices];
+cudaError_t g_scratch_err[kMaxDevices];
+std::once_flag g_scratch_once[kMaxDevices];
+
+// Device address of the scratch array on the current device (looked up once).
+int scratch_address(float **out) {
+  int dev = 0;
+  const cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return capi_fail(static_cast<int>(e), "cudaGetDevice failed");
+  if (dev < 0 || dev >= kMaxDevices) return capi_fail(MI_ERR_UNSUPPORTED, "device index >= 64");
+  std::call_once(g_scratch_once[dev], [dev] {
+    void *ptr = nullptr;
+    g_scratch_err[dev] = cudaGetSymbolAddress(&ptr, g_decode_scratch);
+    g_scratch_ptr[dev] = static_cast<float *>(ptr);
+  });
+  if (g_scratch_err[dev] != cudaSuccess || g_scratch_ptr[dev] == nullptr)
+    return capi_fail(static_cast<int>(g_scratch_err[dev] != cudaSuccess ? g_scratch_err[dev]
+                                                                        : cudaErrorInvalidSymbol),
+                     "cudaGetSymbolAddress of the decode scratch array failed");
+  *out = g_scratch_ptr[dev];
+  return MI_OK;
+}
+
+}  // namespace
+}  // namespace mi
+
+using namespace mi;
+
+extern "C" int mi_paged_decode_noalloc(void *out, const void *query, const void *key_cache,
+                                       const void *value_cache, int64_t num_blocks,
+                                       int32_t block_size, int32_t num_q_heads,
+                                       int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                                       const int32_t *block_tables, int64_t block_table_stride,
+                                       const int32_t *context_lens, int64_t num_seqs, float scale,
+                                       int32_t num_splits, int32_t *dev_status, void *stream) {
+  if (dtype != MI_DTYPE_FLOAT32 && dtype != MI_DTYPE_FLOAT16 && dtype != MI_DTYPE_BFLOAT16)
+    return capi_fail(MI_ERR_INVALID, "unknown dtype");
+  if (num_seqs < 0) return capi_fail(MI_ERR_INVALID, "num_seqs must be >= 0");
+  if (num_blocks <= 0 || block_size <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0)
+    return capi_fail(MI_ERR_INVALID, "cache dimensions must be positive");
+  if (num_q_heads % num_kv_heads != 0)
+    return capi_fail(MI_ERR_INVALID, "num_q_heads must be divisible by num_kv_heads");
+  if (head_dim > 256) return capi_fail(MI_ERR_UNSUPPORTED, "head_dim > 256");
+  if (block_table_stride < 0) return capi_fail(MI_ERR_INVALID, "block_table_stride must be >= 0");
+  if (num_splits < 0 || num_splits > 1024)
+    return capi_fail(MI_ERR_INVALID, "num_splits out of range");
+  if (num_seqs > 65535) return capi_fail(MI_ERR_UNSUPPORTED, "more than 65535 sequences in one call");
+  if (num_seqs == 0) return MI_OK;
+  if (!out || !query || !key_cache || !value_cache || !block_tables || !context_lens)
+    return capi_fail(MI_ERR_INVALID, "null pointer");
+  if (const int s = capi_select_device(key_cache)) return s;
+
+  const int G = num_q_heads / num_kv_heads;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float scale_log2 = scale * 1.4426950408889634f;
+  const bool fast = decode_fast_supported(dtype, head_dim, G) &&
+                    (reinterpret_cast<uintptr_t>(key_cache) & 15u) == 0 &&
+                    (reinterpret_cast<uintptr_t>(value_cache) & 15u) == 0 &&
+                    (reinterpret_cast<uintptr_t>(query) & 15u) == 0;
+  if (!fast) {  // the generic kernel needs no scratch at all
+    AttnParams p = {};
+    p.out = out;
+    p.query = query;
+    p.key_base = static_cast<const char *>(key_cache);
+    p.value_base = static_cast<const char *>(value_cache);
+    p.block_tables = block_tables;
+    p.bt_stride = block_table_stride;
+    p.num_blocks = num_blocks;
+    p.block_size = block_size;
+    p.context_lens = context_lens;
+    p.num_seqs = num_seqs;
+    p.num_tokens = num_seqs;
+    p.num_q_heads = num_q_heads;
+    p.num_kv_heads = num_kv_heads;
+    p.head_dim = head_dim;
+    p.scale_log2 = scale_log2;
+    p.status = dev_status;
+    const cudaError_t e = launch_attn_generic(p, dtype, true, st);
+    return e == cudaSuccess ? MI_OK : capi_fail(static_cast<int>(e), cudaGetErrorString(e));
+  }
+
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int nsplit =
+      num_splits == 0 ? mi_paged_decode_default_splits(num_seqs, num_kv_heads, 0, dev) : num_splits;
+  DecodeParams p = {};
+  p.out = out;
+  p.query = query;
+  p.key_cache = static_cast<const char *>(key_cache);
+  p.value_cache = static_cast<const char *>(value_cache);
+  p.block_tables = block_tables;
+  p.context_lens = context_lens;
+  p.bt_stride = block_table_stride;
+  p.num_blocks = num_blocks;
+  p.block_size = block_size;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.scale_log2 = scale_log2;
+  p.status = dev_status;
+  if (nsplit > 1) {
+    const size_t need = mi_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, nsplit);
+    if (need > kNoAllocScratchBytes)
+      return capi_fail(MI_ERR_INVALID,
+                       "split-K state exceeds the 2 MiB built-in scratch of "
+                       "mi_paged_decode_noalloc (num_seqs * num_q_heads * num_splits * "
+                       "(head_dim + 2) * 4 bytes); use fewer splits or mi_paged_decode");
+    float *scratch = nullptr;
+    if (const int s = scratch_address(&scratch)) return s;
+    const size_t states = static_cast<size_t>(num_seqs) * num_q_heads * nsplit;
+    p.ws_acc = scratch;
+    p.ws_ml = scratch + states * head_dim;
+  }
+  const cudaError_t e = launch_decode_fast(p, dtype, head_dim, G, num_seqs, nsplit, st);
+  return e == cudaSuccess ? MI_OK : capi_fail(static_cast<int>(e), cudaGetErrorString(e));
+}
