@@ -169,6 +169,62 @@ def cpu_baseline(seconds: float = 12.0):
             "ms_per_28_layer_step": round(el / layers_done * LAYERS * 1e3, 3)}
 
 
+def measure_long_b1(device, reps: int = 20):
+    """BASELINE configs[4] run (b): one Qwen3-8B-shaped sequence at 32768 context.
+
+    36 distinct layer pools (36 x 134 MB), store+decode per layer, the split-K
+    path with a workspace; returns decode GB/s over a 36-layer graph replay.
+    """
+    import torch
+
+    import microinfer_b200 as mi
+
+    layers, hq, hkv, ctx_len = 36, 32, 8, 32768
+    nb = ctx_len // BS
+    pool = mi.KVCache(layers, nb, BS, hkv, D, dtype=torch.bfloat16, device=device)
+    g = torch.Generator(device=device).manual_seed(5)
+    pool.keys.normal_(generator=g).mul_(0.5)
+    pool.values.normal_(generator=g).mul_(0.5)
+    table = torch.randperm(nb, generator=g, device=device).to(torch.int32).view(1, nb)
+    ctx = torch.tensor([ctx_len], dtype=torch.int32, device=device)
+    slots = (table[0, -1].long() * BS + BS - 1).to(torch.int32).view(1)
+    q = torch.randn(layers, 1, hq, D, generator=g, device=device).to(torch.bfloat16)
+    kn = torch.randn(layers, 1, hkv, D, generator=g, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    split = mi.select_split_k(1, hkv, device)
+    views = [pool.layer(i) for i in range(layers)]
+
+    def run():
+        for i, view in enumerate(views):
+            mi.paged_decode_store(q[i], view.keys, view.values, table, ctx, kn[i], kn[i], slots,
+                                  split_k=split, out=out[i])
+
+    run()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run()
+    for _ in range(3):
+        graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / reps
+    from oracle.paged_oracle import decode_bytes, store_bytes
+
+    b = layers * (decode_bytes([ctx_len], hq, hkv, D, 2, BS) + store_bytes(1, hkv, D, 2))
+    del graph, pool
+    peaks, src = _peaks()
+    gbs = b / (ms * 1e-3) / 1e9
+    return {"workload": "BASELINE configs[4] run (b): batch 1, context 32768, 32q/8kv, D128, "
+                        "36 layers, bs16", "split_k": split, "ms_per_step": round(ms, 4),
+            "value": round(gbs, 1), "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+            "peak_source": f"hbm_gbs of {src}", "tok_per_s": round(1000.0 / ms, 1)}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -227,18 +283,18 @@ def run_ours(args):
     split = mi.select_split_k(NSEQ, HKV, device)
     views = [pool.layer(i) for i in range(LAYERS)]
 
-    def layer_loop():
+    def attention_layers():
+        # store_kvcache fused into paged decode: one launch per layer
         for i, view in enumerate(views):
-            view.write_slots(slots_d, kn[i], vn[i])
-            mi.paged_decode(q[i], view.keys, view.values, table_d, ctx_d, split_k=split,
-                            out=out[i])
+            mi.paged_decode_store(q[i], view.keys, view.values, table_d, ctx_d, kn[i], vn[i],
+                                  slots_d, split_k=split, out=out[i])
+
+    def layer_loop():
+        attention_layers()
         # stand-in sampler: one int32 token id per sequence from the last layer
         tokens.copy_(out[-1, :, 0, :].float().argmax(-1))
 
-    def decode_only():
-        for i, view in enumerate(views):
-            mi.paged_decode(q[i], view.keys, view.values, table_d, ctx_d, split_k=split,
-                            out=out[i])
+    decode_only = attention_layers
 
     # warm up + capture
     stream = torch.cuda.Stream(device)
@@ -313,7 +369,7 @@ def run_ours(args):
     torch.cuda.synchronize(device)
     decode_launch_ms = e0.elapsed_time(e1) / (reps * LAYERS)
     peaks, peak_src = _peaks()
-    achieved = dec_b / (decode_launch_ms * 1e-3) / 1e9
+    achieved = (dec_b + st_b) / (decode_launch_ms * 1e-3) / 1e9
 
     # --- e2e: host buffers through the public API ----------------------------
     h_q = torch.empty_like(q, device="cpu").pin_memory()
@@ -356,7 +412,8 @@ def run_ours(args):
     e2e_value = world * step_bytes / (e2e_ms * 1e-3) / 1e9
     mi.check_device_status(device)
 
-    launches_per_step = LAYERS * (2 + (1 if split > 1 else 0))
+    uses_ws = bool(mi.load().mi_paged_decode_uses_workspace(split))
+    launches_per_step = LAYERS * (1 + (1 if uses_ws else 0))
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
@@ -372,13 +429,14 @@ def run_ours(args):
                        "graph": "28-layer store+decode CUDA graph replay"},
             "tok_per_s": round(world * NSEQ / (ms_step * 1e-3), 1),
             "median_step_ms": round(statistics.median(per_step), 5),
-            "roofline": {"bound": "hbm", "kernel": "paged_decode_kernel (+combine)",
+            "roofline": {"bound": "hbm",
+                         "kernel": "paged_decode_kernel (store fused, cluster split merge)",
                          "achieved": round(achieved, 1),
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "peak_source": f"hbm_gbs of {peak_src}",
                          "avg_launch_us": round(decode_launch_ms * 1e3, 3),
-                         "algorithmic_bytes_per_launch": dec_b, "traffic": None,
+                         "algorithmic_bytes_per_launch": dec_b + st_b, "traffic": None,
                          "step_frac": round(value / world / peaks["hbm_gbs"], 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
@@ -386,6 +444,8 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
         }
+        if world == 1:
+            line["extra"] = {"long_context_b1": measure_long_b1(device)}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
@@ -420,8 +480,8 @@ def run_profile(args):
     for _ in range(args.steps):
         for i in range(layers):
             view = pool.layer(i)
-            view.write_slots(slots_d, kn[i], kn[i])
-            mi.paged_decode(q[i], view.keys, view.values, table_d, ctx_d, split_k=split)
+            mi.paged_decode_store(q[i], view.keys, view.values, table_d, ctx_d, kn[i], kn[i],
+                                  slots_d, split_k=split)
     torch.cuda.synchronize(device)
     mi.check_device_status(device)
     dec_b, _ = algorithmic_bytes(ctx.tolist())

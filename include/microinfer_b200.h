@@ -125,8 +125,10 @@ MI_API int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads
  * with GQA kv head h / (num_q_heads / num_kv_heads).  Replaces
  * triton_paged_decode + _paged_decode_kernel + _paged_decode_reduce_kernel,
  * microinfer/layer/triton_paged_attention.py:352-457 (:39-131, :235-257).
- * num_splits > 1 uses `workspace` (mi_paged_decode_workspace_bytes) and a
- * combine kernel; num_splits == 0 picks mi_paged_decode_default_splits.
+ * num_splits > 8 uses `workspace` (mi_paged_decode_workspace_bytes) and a
+ * combine kernel, 2..8 splits merge in a thread-block cluster (see
+ * mi_paged_decode_uses_workspace); num_splits == 0 picks
+ * mi_paged_decode_default_splits.
  * Query and out are contiguous [num_seqs, num_q_heads, head_dim].
  */
 MI_API int mi_paged_decode(void *out, const void *query, const void *key_cache,
@@ -137,6 +139,39 @@ MI_API int mi_paged_decode(void *out, const void *query, const void *key_cache,
                     const int32_t *context_lens, int64_t num_seqs, float scale,
                     int32_t num_splits, void *workspace,
                     size_t workspace_bytes, int32_t *dev_status, void *stream);
+
+/*
+ * 1 when mi_paged_decode needs a workspace for `num_splits` splits, else 0.
+ * With 2..8 splits the splits of one (sequence, kv head) run as a thread
+ * block cluster and merge through distributed shared memory, so no
+ * workspace and no combine launch are needed (environment variable
+ * MICROINFER_B200_CLUSTER=0 turns this off).
+ */
+MI_API int mi_paged_decode_uses_workspace(int32_t num_splits);
+
+/*
+ * Paged decode with this step's store_kvcache fused in: for each sequence s
+ * with slot_mapping[s] >= 0, k_new/v_new row s ([num_kv_heads, head_dim],
+ * rows new_token_stride elements apart) is written to that slot of the pool,
+ * then decode runs exactly as mi_paged_decode.  slot_mapping[s] must address
+ * position context_lens[s]-1 of sequence s (the reference's decode contract,
+ * microinfer/runner.py:160-177).  Replaces the LayerKVCache.write_fast +
+ * paged_attention_meta pair of CachedAttention.forward for decode
+ * (microinfer/layer/cached_attention.py:76-85) with one launch.
+ */
+MI_API int mi_paged_decode_store(void *out, const void *query, void *key_cache,
+                          void *value_cache, int64_t num_blocks,
+                          int32_t block_size, int32_t num_q_heads,
+                          int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                          const int32_t *block_tables,
+                          int64_t block_table_stride,
+                          const int32_t *context_lens, int64_t num_seqs,
+                          const void *k_new, const void *v_new,
+                          int64_t new_token_stride,
+                          const int32_t *slot_mapping, float scale,
+                          int32_t num_splits, void *workspace,
+                          size_t workspace_bytes, int32_t *dev_status,
+                          void *stream);
 
 /*
  * Allocation-free paged decode.  No counterpart in the reference: it exists

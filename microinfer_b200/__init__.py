@@ -22,6 +22,7 @@ from microinfer_b200.layer.paged_attention import (
     gather_paged_kv,
     paged_attention_meta,
     paged_decode,
+    paged_decode_store,
     paged_prefill,
     select_split_k,
     varlen_prefill,
@@ -40,6 +41,7 @@ __all__ = [
     "load",
     "paged_attention_meta",
     "paged_decode",
+    "paged_decode_store",
     "paged_prefill",
     "read_device_status",
     "select_split_k",

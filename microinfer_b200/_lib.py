@@ -49,6 +49,12 @@ SIGNATURES = {
         [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _F, _I32, _P,
          _SZ, _P, _P],
     ),
+    "mi_paged_decode_uses_workspace": (ctypes.c_int, [_I32]),
+    "mi_paged_decode_store": (
+        ctypes.c_int,
+        [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _P, _P, _I64, _P,
+         _F, _I32, _P, _SZ, _P, _P],
+    ),
     "mi_paged_decode_noalloc": (
         ctypes.c_int,
         [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _F, _I32, _P,

@@ -216,12 +216,35 @@ int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads, int32
   return static_cast<int>(s);
 }
 
-int mi_paged_decode(void *out, const void *query, const void *key_cache, const void *value_cache,
-                    int64_t num_blocks, int32_t block_size, int32_t num_q_heads,
-                    int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
-                    const int32_t *block_tables, int64_t block_table_stride,
-                    const int32_t *context_lens, int64_t num_seqs, float scale, int32_t num_splits,
-                    void *workspace, size_t workspace_bytes, int32_t *dev_status, void *stream) {
+}  // extern "C"
+
+namespace {
+
+bool cluster_enabled() {
+  static const bool enabled = [] {
+    const char *v = std::getenv("MICROINFER_B200_CLUSTER");
+    return !(v != nullptr && std::strcmp(v, "0") == 0);
+  }();
+  return enabled;
+}
+
+// 2..8 splits merge through a thread-block cluster (no workspace); more
+// splits (or clusters switched off) use the workspace + combine kernel.
+bool decode_uses_workspace(int nsplit) { return nsplit > 1 && !(cluster_enabled() && nsplit <= 8); }
+
+struct NewToken {
+  const void *k_new;
+  const void *v_new;
+  int64_t stride;  // elements between sequences' rows
+  const int32_t *slots;
+};
+
+int decode_impl(void *out, const void *query, const void *key_cache, const void *value_cache,
+                int64_t num_blocks, int32_t block_size, int32_t num_q_heads, int32_t num_kv_heads,
+                int32_t head_dim, int32_t dtype, const int32_t *block_tables,
+                int64_t block_table_stride, const int32_t *context_lens, int64_t num_seqs,
+                const NewToken *nt, float scale, int32_t num_splits, void *workspace,
+                size_t workspace_bytes, int32_t *dev_status, void *stream) {
   const int e = elem_size(dtype);
   if (e == 0) return fail(MI_ERR_INVALID, "unknown dtype");
   if (num_seqs < 0) return fail(MI_ERR_INVALID, "num_seqs must be >= 0");
@@ -236,7 +259,9 @@ int mi_paged_decode(void *out, const void *query, const void *key_cache, const v
   if (num_seqs == 0) return MI_OK;
   if (!out || !query || !key_cache || !value_cache || !block_tables || !context_lens)
     return fail(MI_ERR_INVALID, "null pointer");
-  if (num_splits > 1 &&
+  if (nt != nullptr && (!nt->k_new || !nt->v_new || !nt->slots || nt->stride < 0))
+    return fail(MI_ERR_INVALID, "fused store needs k_new, v_new, slot_mapping and a stride >= 0");
+  if (decode_uses_workspace(num_splits) &&
       (workspace == nullptr ||
        workspace_bytes < mi_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, num_splits)))
     return fail(MI_ERR_INVALID, "workspace too small for num_splits (see "
@@ -246,6 +271,29 @@ int mi_paged_decode(void *out, const void *query, const void *key_cache, const v
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool fast = decode_fast_supported(dtype, head_dim, G) && aligned16(key_cache) &&
                     aligned16(value_cache) && aligned16(query);
+  // The fused store reads k_new/v_new rows with 16-byte loads.
+  const bool fuse_store = nt != nullptr && fast && aligned16(nt->k_new) && aligned16(nt->v_new) &&
+                          (nt->stride * e) % 16 == 0;
+  if (nt != nullptr && !fuse_store) {  // store first, as its own launch
+    StoreParams sp;
+    sp.key_cache = static_cast<char *>(const_cast<void *>(key_cache));
+    sp.value_cache = static_cast<char *>(const_cast<void *>(value_cache));
+    sp.keys = static_cast<const char *>(nt->k_new);
+    sp.values = static_cast<const char *>(nt->v_new);
+    sp.idx0 = nt->slots;
+    sp.idx1 = nullptr;
+    sp.num_blocks = num_blocks;
+    sp.num_tokens = num_seqs;
+    sp.key_stride_bytes = nt->stride * e;
+    sp.value_stride_bytes = nt->stride * e;
+    sp.block_size = block_size;
+    sp.row_bytes = num_kv_heads * head_dim * e;
+    sp.status = dev_status;
+    const bool vec16 = sp.row_bytes % 16 == 0 && aligned16(key_cache) && aligned16(value_cache) &&
+                       aligned16(nt->k_new) && aligned16(nt->v_new) && sp.key_stride_bytes % 16 == 0;
+    const cudaError_t se = launch_store_kv(sp, MI_INDEX_INT32, true, e, vec16, st);
+    if (se != cudaSuccess) return cuda_status(se);
+  }
   if (!fast) {
     AttnParams p = {};
     p.out = out;
@@ -284,7 +332,13 @@ int mi_paged_decode(void *out, const void *query, const void *key_cache, const v
   p.num_kv_heads = num_kv_heads;
   p.scale_log2 = scale * kLog2eHost;
   p.status = dev_status;
-  if (nsplit > 1) {
+  if (fuse_store) {
+    p.k_new = static_cast<const char *>(nt->k_new);
+    p.v_new = static_cast<const char *>(nt->v_new);
+    p.slot_mapping = nt->slots;
+    p.new_token_stride_bytes = nt->stride * e;
+  }
+  if (decode_uses_workspace(nsplit)) {
     const size_t need = mi_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, nsplit);
     if (workspace == nullptr || workspace_bytes < need)
       return fail(MI_ERR_INVALID, "workspace too small for num_splits (see "
@@ -294,8 +348,46 @@ int mi_paged_decode(void *out, const void *query, const void *key_cache, const v
     const size_t states = static_cast<size_t>(num_seqs) * num_q_heads * nsplit;
     p.ws_acc = static_cast<float *>(workspace);
     p.ws_ml = p.ws_acc + states * head_dim;
+  } else if (nsplit > 1) {
+    p.cluster_combine = 1;
   }
   return cuda_status(launch_decode_fast(p, dtype, head_dim, G, num_seqs, nsplit, st));
+}
+
+}  // namespace
+
+extern "C" {
+
+int mi_paged_decode_uses_workspace(int32_t num_splits) {
+  return decode_uses_workspace(num_splits) ? 1 : 0;
+}
+
+int mi_paged_decode(void *out, const void *query, const void *key_cache, const void *value_cache,
+                    int64_t num_blocks, int32_t block_size, int32_t num_q_heads,
+                    int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                    const int32_t *block_tables, int64_t block_table_stride,
+                    const int32_t *context_lens, int64_t num_seqs, float scale, int32_t num_splits,
+                    void *workspace, size_t workspace_bytes, int32_t *dev_status, void *stream) {
+  return decode_impl(out, query, key_cache, value_cache, num_blocks, block_size, num_q_heads,
+                     num_kv_heads, head_dim, dtype, block_tables, block_table_stride, context_lens,
+                     num_seqs, nullptr, scale, num_splits, workspace, workspace_bytes, dev_status,
+                     stream);
+}
+
+int mi_paged_decode_store(void *out, const void *query, void *key_cache, void *value_cache,
+                          int64_t num_blocks, int32_t block_size, int32_t num_q_heads,
+                          int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                          const int32_t *block_tables, int64_t block_table_stride,
+                          const int32_t *context_lens, int64_t num_seqs, const void *k_new,
+                          const void *v_new, int64_t new_token_stride,
+                          const int32_t *slot_mapping, float scale, int32_t num_splits,
+                          void *workspace, size_t workspace_bytes, int32_t *dev_status,
+                          void *stream) {
+  const NewToken nt{k_new, v_new, new_token_stride, slot_mapping};
+  return decode_impl(out, query, key_cache, value_cache, num_blocks, block_size, num_q_heads,
+                     num_kv_heads, head_dim, dtype, block_tables, block_table_stride, context_lens,
+                     num_seqs, &nt, scale, num_splits, workspace, workspace_bytes, dev_status,
+                     stream);
 }
 
 static int prefill_common(void *out, const void *query, const void *kbase, const void *vbase,

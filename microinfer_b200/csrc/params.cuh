@@ -83,6 +83,14 @@ struct DecodeParams {
   int32_t num_kv_heads;
   float scale_log2;
   int32_t *status;
+  // Fused store_kvcache of this step's token (k_new == nullptr: no store).
+  const char *k_new;  // [num_seqs, Hkv, D] rows at new_token_stride_bytes
+  const char *v_new;
+  const int32_t *slot_mapping;  // int32 [num_seqs]; -1 = padding row, no store
+  int64_t new_token_stride_bytes;
+  // 1: the splits of one (seq, kv head) form a thread-block cluster and are
+  // merged through distributed shared memory (no workspace, no combine launch).
+  int32_t cluster_combine;
 };
 
 }  // namespace mi

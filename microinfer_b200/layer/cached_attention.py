@@ -12,7 +12,11 @@ from __future__ import annotations
 import torch
 from torch import nn
 
-from microinfer_b200.layer.paged_attention import paged_attention_meta, varlen_prefill
+from microinfer_b200.layer.paged_attention import (
+    paged_attention_meta,
+    paged_decode_store,
+    varlen_prefill,
+)
 from microinfer_b200.worker.kv_cache import LayerKVCache
 
 
@@ -33,6 +37,11 @@ class CachedAttention(nn.Module):
         if cache is not None:
             if metadata.slot_mapping is None:
                 raise ValueError("bound cache requires slot_mapping")
+            if (metadata.is_decode and not metadata.validate_cache_write
+                    and metadata.context_lens is not None):
+                # One launch: store this step's K/V, then decode over the cache.
+                return paged_decode_store(q, cache.keys, cache.values, metadata.block_tables,
+                                          metadata.context_lens, k, v, metadata.slot_mapping)
             if metadata.validate_cache_write:
                 cache.write_checked(metadata.slot_mapping, k, v)
             else:

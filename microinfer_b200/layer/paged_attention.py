@@ -66,14 +66,9 @@ def select_split_k(num_requests: int, num_kv_heads: int, device=None,
     return _lib.load().mi_paged_decode_default_splits(num_requests, num_kv_heads, max_context, dev)
 
 
-def paged_decode(query, key_cache, value_cache, block_tables, context_lens, *,
-                 scale: float | None = None, split_k: int | None = None,
-                 out: torch.Tensor | None = None) -> torch.Tensor:
-    """One query token per request over its paged KV (any block size)."""
+def _decode_prep(query, key_cache, value_cache, block_tables, context_lens, split_k, scale, out):
     num_q_heads, head_dim, block_size, num_kv_heads = _check_common(query, key_cache, value_cache)
     num_requests = query.shape[0]
-    if num_requests == 0:
-        return torch.empty_like(query)
     device = _lib.require_cuda(query, key_cache, value_cache, block_tables, context_lens)
     if block_tables.ndim != 2 or block_tables.shape[0] != num_requests:
         raise ValueError("block_tables must have one row per request")
@@ -83,29 +78,76 @@ def paged_decode(query, key_cache, value_cache, block_tables, context_lens, *,
         split_k = select_split_k(num_requests, num_kv_heads, device)
     if type(split_k) is not int or split_k <= 0:
         raise ValueError("split_k must be a positive int")
-    query = query.contiguous()
-    key_cache = key_cache.contiguous()
-    value_cache = value_cache.contiguous()
-    block_tables = _idx(block_tables)
-    context_lens = _idx(context_lens)
-    if out is None:
-        out = torch.empty_like(query)
-    if scale is None:
-        scale = 1.0 / math.sqrt(head_dim)
+    if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
+        raise ValueError("KV caches must be contiguous")
     lib = _lib.load()
-    ws_bytes = lib.mi_paged_decode_workspace_bytes(num_requests, num_q_heads, head_dim, split_k)
+    ws_bytes = 0
     workspace = None
-    if ws_bytes:
+    if lib.mi_paged_decode_uses_workspace(split_k):
+        ws_bytes = lib.mi_paged_decode_workspace_bytes(num_requests, num_q_heads, head_dim, split_k)
         workspace = torch.empty(ws_bytes // 4, dtype=torch.float32, device=device)
-    _lib.call(
-        "mi_paged_decode", out.data_ptr(), query.data_ptr(), key_cache.data_ptr(),
-        value_cache.data_ptr(), key_cache.shape[0], block_size, num_q_heads, num_kv_heads,
-        head_dim, _lib.dtype_code(query.dtype), block_tables.data_ptr(), block_tables.stride(0),
-        context_lens.data_ptr(), num_requests, float(scale), split_k,
-        _lib.ptr(workspace), ws_bytes, _lib.status_buffer(device).data_ptr(),
-        _lib.stream_of(device),
+    return dict(
+        query=query.contiguous(), block_tables=_idx(block_tables), context_lens=_idx(context_lens),
+        out=torch.empty_like(query) if out is None else out, device=device, split_k=split_k,
+        scale=1.0 / math.sqrt(head_dim) if scale is None else float(scale),
+        workspace=workspace, ws_bytes=ws_bytes,
+        dims=(key_cache.shape[0], block_size, num_q_heads, num_kv_heads, head_dim,
+              _lib.dtype_code(query.dtype)),
     )
-    return out
+
+
+def paged_decode(query, key_cache, value_cache, block_tables, context_lens, *,
+                 scale: float | None = None, split_k: int | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """One query token per request over its paged KV (any block size)."""
+    if query.shape[0] == 0:
+        return torch.empty_like(query)
+    a = _decode_prep(query, key_cache, value_cache, block_tables, context_lens, split_k, scale, out)
+    _lib.call(
+        "mi_paged_decode", a["out"].data_ptr(), a["query"].data_ptr(), key_cache.data_ptr(),
+        value_cache.data_ptr(), *a["dims"], a["block_tables"].data_ptr(),
+        a["block_tables"].stride(0), a["context_lens"].data_ptr(), query.shape[0], a["scale"],
+        a["split_k"], _lib.ptr(a["workspace"]), a["ws_bytes"],
+        _lib.status_buffer(a["device"]).data_ptr(), _lib.stream_of(a["device"]),
+    )
+    return a["out"]
+
+
+def paged_decode_store(query, key_cache, value_cache, block_tables, context_lens, k_new, v_new,
+                       slot_mapping, *, scale: float | None = None, split_k: int | None = None,
+                       out: torch.Tensor | None = None) -> torch.Tensor:
+    """store_kvcache of this step's token fused into paged decode (one launch).
+
+    ``k_new``/``v_new`` are ``[requests, Hkv, D]`` (inner dims contiguous);
+    ``slot_mapping[r]`` (-1 = padding) must address position
+    ``context_lens[r] - 1`` of request r, as the reference runner builds it.
+    """
+    if query.shape[0] == 0:
+        return torch.empty_like(query)
+    n = query.shape[0]
+    if k_new.shape != (n, *key_cache.shape[2:]) or v_new.shape != k_new.shape:
+        raise ValueError("k_new/v_new must be [requests, Hkv, D]")
+    if k_new.dtype != key_cache.dtype or v_new.dtype != key_cache.dtype:
+        raise ValueError("k_new/v_new dtype must match the cache")
+    if k_new.stride(-1) != 1 or k_new.stride(-2) != k_new.shape[-1]:
+        k_new = k_new.contiguous()
+    if v_new.stride() != k_new.stride():
+        v_new = v_new.contiguous()
+        k_new = k_new.contiguous()
+    if slot_mapping.shape != (n,):
+        raise ValueError("slot_mapping must have one entry per request")
+    _lib.require_cuda(k_new, v_new, slot_mapping)
+    a = _decode_prep(query, key_cache, value_cache, block_tables, context_lens, split_k, scale, out)
+    slots = _idx(slot_mapping)
+    _lib.call(
+        "mi_paged_decode_store", a["out"].data_ptr(), a["query"].data_ptr(), key_cache.data_ptr(),
+        value_cache.data_ptr(), *a["dims"], a["block_tables"].data_ptr(),
+        a["block_tables"].stride(0), a["context_lens"].data_ptr(), n, k_new.data_ptr(),
+        v_new.data_ptr(), k_new.stride(0), slots.data_ptr(), a["scale"], a["split_k"],
+        _lib.ptr(a["workspace"]), a["ws_bytes"], _lib.status_buffer(a["device"]).data_ptr(),
+        _lib.stream_of(a["device"]),
+    )
+    return a["out"]
 
 
 def paged_prefill(query, key_cache, value_cache, cu_seqlens_q, cu_seqlens_k, block_tables, *,

@@ -70,7 +70,7 @@ def _decode_args(**over):
     (dict(dtype=7), "dtype"),
     (dict(head_dim=512), "head_dim"),
     (dict(num_splits=-1), "num_splits"),
-    (dict(num_splits=4, workspace=None, workspace_bytes=0), "workspace"),
+    (dict(num_splits=16, workspace=None, workspace_bytes=0), "workspace"),
     (dict(out=None), "null"),
 ])
 def test_decode_rejects_invalid_arguments_before_launch(over, fragment):
@@ -80,6 +80,11 @@ def test_decode_rejects_invalid_arguments_before_launch(over, fragment):
     assert fragment in lib.mi_last_error().decode()
     with pytest.raises(ValueError):
         _lib.check(status)
+
+
+def test_workspace_needed_only_beyond_cluster_merge():
+    lib = _lib.load()
+    assert [lib.mi_paged_decode_uses_workspace(s) for s in (1, 2, 8, 9, 37)] == [0, 0, 0, 1, 1]
 
 
 def test_decode_with_no_sequences_is_a_no_op():

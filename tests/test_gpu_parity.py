@@ -125,6 +125,41 @@ def test_decode_split_k_matches_reference(name, split_k):
     assert_close(out, gold["out"], dt)
 
 
+@pytest.mark.parametrize("name", [c for c in PAGED if cases.kind(c) == "decode"])
+@pytest.mark.parametrize("split_k", [1, 4, 16])
+def test_fused_store_decode_matches_reference(name, split_k):
+    """store_kvcache fused into the decode launch: same cache bytes, same output."""
+    case = cases.build(name)
+    gold = load_golden(name)
+    dt = case["dtype"]
+    kc, vc = dev(case["key_cache"], dt), dev(case["value_cache"], dt)
+    out = mi.paged_decode_store(dev(case["query"], dt), kc, vc, dev(case["block_tables"]),
+                                dev(case["contexts"]), dev(case["k_new"], dt),
+                                dev(case["v_new"], dt), dev(case["slots"]), scale=case["scale"],
+                                split_k=split_k)
+    slots = case["slots"].astype(np.int64)
+    bs = case["block_size"]
+    np.testing.assert_array_equal(host(kc, dt)[slots // bs, slots % bs], gold["stored_k"])
+    np.testing.assert_array_equal(host(vc, dt)[slots // bs, slots % bs], gold["stored_v"])
+    assert_close(out, gold["out"], dt)
+
+
+def test_fused_store_skips_padding_slots():
+    case = cases.build("cfg2_layer_bf16")
+    dt = "bf16"
+    kc, vc = dev(case["key_cache"], dt), dev(case["value_cache"], dt)
+    before = host(kc, dt)
+    slots = dev(case["slots"])
+    slots[0] = -1  # padding row: nothing written for sequence 0
+    mi.paged_decode_store(dev(case["query"], dt), kc, vc, dev(case["block_tables"]),
+                          dev(case["contexts"]), dev(case["k_new"], dt), dev(case["v_new"], dt),
+                          slots, split_k=4)
+    s0 = int(case["slots"][0])
+    np.testing.assert_array_equal(host(kc, dt)[s0 // 16, s0 % 16], before[s0 // 16, s0 % 16])
+    s1 = int(case["slots"][1])
+    np.testing.assert_array_equal(host(kc, dt)[s1 // 16, s1 % 16], case["k_new"][1])
+
+
 @pytest.mark.parametrize("name", ["cfg1_decode_f32", "cfg2_layer_bf16", "decode_bs64_bf16"])
 def test_decode_kernel_agrees_with_prefill_kernel(name):
     """The decode kernels and the varlen prefill kernels are separate code."""
