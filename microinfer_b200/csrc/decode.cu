@@ -46,7 +46,7 @@ struct DecCfg {
   static constexpr int kCPL = kChunks > 32 ? kChunks / 32 : 1;    // chunks per lane per row
   static constexpr int kLPR = kChunks / kCPL;                     // lanes per row
   static constexpr int kRPS = 32 / kLPR;                          // lane groups (rows in flight)
-  static constexpr int kKeys = 16;                                // keys per stage
+  static constexpr int kKeys = 8;                                 // keys per stage
   static constexpr int kKPG = kKeys / kRPS;                       // keys per lane group
   static constexpr int kEPL = kCPL * kVec;                        // elements per lane per row
   static constexpr int kSub = (kKPG * G <= 32) ? kKPG : (32 / G > 0 ? 32 / G : 1);
@@ -55,8 +55,9 @@ struct DecCfg {
   static constexpr int kF = kV0 >= kLPR ? kV0 / kLPR : 1;    // reduced dots kept per lane
   static constexpr int kDup = kV0 >= kLPR ? 1 : kLPR / kV0;  // lanes holding the same dot
   static constexpr int kStageBytes = kKeys * 2 * kRowBytes;
-  static constexpr int kStages = kStageBytes <= 8192 ? 3 : 2;
-  static constexpr int kWarps = 4;
+  static constexpr int kStages = kStageBytes <= 4096 ? 3 : 2;
+  static constexpr int kWarps = 8;
+  static constexpr int kThreads = kWarps * 32;
   static constexpr int kSmemStages = kWarps * kStages * kStageBytes;
   static constexpr int kSmemP = kWarps * kKeys * G * 4;
   static constexpr int kSmemBars = kWarps * kStages * 8;
@@ -97,7 +98,7 @@ __device__ __forceinline__ void transpose_reduce(float (&v)[N], int c) {
 }
 
 template <typename T, int D, int G>
-__global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
+__global__ void __launch_bounds__(256, G >= 8 ? 1 : 2) paged_decode_kernel(DecodeParams p) {
   using C = DecCfg<T, D, G>;
   extern __shared__ __align__(128) char smem[];
   char *stage_mem = smem;
@@ -112,7 +113,10 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
   uint64_t *wbar = bars + warp * C::kStages;
   char *wstage = stage_mem + warp * C::kStages * C::kStageBytes;
   float *wp = p_smem + warp * C::kKeys * G;
-  const int copy_key = lane & 15;
+  // Copies: lanes 0-7 fetch the chunk's K rows, lanes 8-15 its V rows.
+  const int copy_key = lane & (C::kKeys - 1);
+  const int copy_kind = (lane / C::kKeys) & 1;
+  const bool copy_lane = lane < 2 * C::kKeys;
   const bool fused = p.k_new != nullptr;
 
   if (lane == 0) {
@@ -150,13 +154,13 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
                         (last_chunk / nsplit) % C::kWarps == warp;
 
   const int64_t tok_bytes = static_cast<int64_t>(p.num_kv_heads) * C::kRowBytes;
-  const char *kv_src_base = ((lane >> 4) ? p.value_cache : p.key_cache) +
+  const char *kv_src_base = (copy_kind ? p.value_cache : p.key_cache) +
                             static_cast<int64_t>(kvh) * C::kRowBytes;
 
   // Validate a prefetched table entry for this lane's row of chunk ci.
   auto check_blk = [&](int ci, int64_t blk) -> int64_t {
     const int key = ci * C::kKeys + copy_key;
-    if (key >= ctx) return -1;
+    if (!copy_lane || key >= ctx) return -1;
     if (blk < 0 || blk >= p.num_blocks) {
       flag_status(p.status, MI_DEV_BAD_BLOCK);
       return -1;
@@ -193,7 +197,7 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
     if (lane == 0) mbar_arrive_expect_tx(&wbar[st], __popc(mask) * C::kRowBytes);
     if (go) {
       const char *src = kv_src_base + (blk * p.block_size + key % p.block_size) * tok_bytes;
-      char *dst = wstage + st * C::kStageBytes + (lane >> 4) * C::kKeys * C::kRowBytes +
+      char *dst = wstage + st * C::kStageBytes + copy_kind * C::kKeys * C::kRowBytes +
                   copy_key * C::kRowBytes;
       bulk_g2s(dst, src, C::kRowBytes, &wbar[st]);
     }
@@ -380,9 +384,10 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
         }
       }
     }
+    // Every lane has consumed its loads from this stage (their values fed the
+    // FMAs above), so the stage can be refilled: no proxy fence needed.
     __syncwarp();
     if (has_next) {
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       issue(nci, st, check_blk(nci, nblk_raw));
       ++issued;
     }
@@ -478,30 +483,39 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(DecodeParams p) {
   }
   if (cluster_merge) {
     // The splits of this (seq, kv head) are the CTAs of one cluster along x.
+    // Each rank finalises a slice of the (head, dim) outputs, issuing all of
+    // its remote (DSMEM) loads before using any of them.
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
-    if (cluster.block_rank() == 0) {
-      for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
-        const int h = i / D, d = i % D;
-        float M = -INFINITY;
-        for (int s = 0; s < nsplit; ++s) {
+    for (int i = split * C::kThreads + threadIdx.x; i < G * D; i += nsplit * C::kThreads) {
+      const int h = i / D, d = i % D;
+      float ms[8], ls[8], as[8];
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        if (s < nsplit) {
           const float *rml = cluster.map_shared_rank(fin_ml, s);
-          M = fmaxf(M, rml[h * 2]);
+          ms[s] = rml[h * 2];
+          ls[s] = rml[h * 2 + 1];
+          as[s] = cluster.map_shared_rank(fin_acc, s)[h * D + d];
         }
-        float L = 0.f, A = 0.f;
-        for (int s = 0; s < nsplit; ++s) {
-          const float *rml = cluster.map_shared_rank(fin_ml, s);
-          const float *racc = cluster.map_shared_rank(fin_acc, s);
-          const float ms = rml[h * 2];
-          const float f = (ms == -INFINITY) ? 0.f : fast_exp2(ms - M);
-          L += f * rml[h * 2 + 1];
-          A += f * racc[h * D + d];
-        }
-        T *o = static_cast<T *>(p.out) + (seq * p.num_q_heads + kvh * G + h) * D;
-        o[d] = Elem<T>::from_float(L > 0.f ? A / L : 0.f);
       }
+      float M = -INFINITY;
+#pragma unroll
+      for (int s = 0; s < 8; ++s)
+        if (s < nsplit) M = fmaxf(M, ms[s]);
+      float L = 0.f, A = 0.f;
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        if (s < nsplit) {
+          const float f = (ms[s] == -INFINITY) ? 0.f : fast_exp2(ms[s] - M);
+          L += f * ls[s];
+          A += f * as[s];
+        }
+      }
+      T *o = static_cast<T *>(p.out) + (seq * p.num_q_heads + kvh * G + h) * D;
+      o[d] = Elem<T>::from_float(L > 0.f ? A / L : 0.f);
     }
-    cluster.sync();  // keep every rank's shared memory alive until rank 0 has read it
+    cluster.sync();  // keep every rank's shared memory alive until all reads are done
   }
 }
 
@@ -549,7 +563,7 @@ static cudaError_t launch_decode_tdg(const DecodeParams &p, int64_t num_seqs, in
   if (p.cluster_combine && nsplit > 1) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(128);
+    cfg.blockDim = dim3(C::kThreads);
     cfg.dynamicSmemBytes = C::kSmem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];
@@ -563,7 +577,7 @@ static cudaError_t launch_decode_tdg(const DecodeParams &p, int64_t num_seqs, in
     cfg.numAttrs = pdl_enabled() ? 2 : 1;
     return cudaLaunchKernelEx(&cfg, kern, p);
   }
-  cudaError_t e = launch_pdl(kern, grid, dim3(128), C::kSmem, stream, p);
+  cudaError_t e = launch_pdl(kern, grid, dim3(C::kThreads), C::kSmem, stream, p);
   if (e != cudaSuccess || nsplit == 1) return e;
   return launch_pdl(decode_combine_kernel<T>, dim3(p.num_q_heads, static_cast<unsigned>(num_seqs)),
                     dim3(128), 0, stream, p, nsplit, D);
