@@ -225,6 +225,116 @@ def measure_long_b1(device, reps: int = 20):
             "peak_source": f"hbm_gbs of {src}", "tok_per_s": round(1000.0 / ms, 1)}
 
 
+def _prefill_batch(workload: str, device, g):
+    """Metadata + per-layer-shaped inputs for BASELINE configs[2] / configs[3]."""
+    import torch
+
+    gen = torch.Generator(device="cpu").manual_seed(3 if workload == "mixed" else 4)
+    if workload == "mixed":
+        # configs[2]: 24 decode sequences ctx U[1,4096] + 8 prefill chunks of 512 on 0..1536 cached
+        dec = torch.randint(1, 4097, (24,), generator=gen)
+        pre_p = torch.randint(0, 1537, (8,), generator=gen)
+        q_lens = [1] * 24 + [512] * 8
+        contexts = dec.tolist() + (pre_p + 512).tolist()
+        need = [(c + BS - 1) // BS for c in contexts]
+        nb = sum(need) + 8
+        perm = torch.randperm(nb, generator=gen).to(torch.int32)
+        table = torch.full((len(contexts), max(need)), -1, dtype=torch.int32)
+        at = 0
+        for r, k in enumerate(need):
+            table[r, :k] = perm[at:at + k]
+            at += k
+    else:
+        # configs[3]: 64 sequences share a 1024-token prefix stored once (64 block ids in
+        # every table); each prefills its own 128-token suffix on top of it
+        n, prefix, suffix = 64, 1024, 128
+        shared = torch.arange(prefix // BS, dtype=torch.int32)
+        q_lens = [suffix] * n
+        contexts = [prefix + suffix] * n
+        per = suffix // BS
+        nb = prefix // BS + n * per + 8
+        table = torch.empty((n, prefix // BS + per), dtype=torch.int32)
+        for r in range(n):
+            table[r, :prefix // BS] = shared
+            table[r, prefix // BS:] = torch.arange(prefix // BS + r * per,
+                                                   prefix // BS + (r + 1) * per)
+    cu_q = torch.tensor([0] + list(torch.cumsum(torch.tensor(q_lens), 0).tolist()), dtype=torch.int32)
+    cu_k = torch.tensor([0] + list(torch.cumsum(torch.tensor(contexts), 0).tolist()), dtype=torch.int32)
+    slots = []
+    for r, (q, c) in enumerate(zip(q_lens, contexts)):
+        for pos in range(c - q, c):
+            slots.append(int(table[r, pos // BS]) * BS + pos % BS)
+    return dict(q_lens=q_lens, contexts=contexts, nb=nb, table=table.to(device),
+                cu_q=cu_q.to(device), cu_k=cu_k.to(device),
+                slots=torch.tensor(slots, dtype=torch.int32, device=device))
+
+
+def measure_prefill(device, workload: str, layers: int = 28, reps: int = 10):
+    """Store + paged prefill per layer (one attention launch for the whole batch).
+
+    mixed  = BASELINE configs[2]: decode rows and prefill chunks in one launch;
+    prefix = BASELINE configs[3]: suffix prefill over a shared, refcounted prefix.
+    Reports prefill TFLOP/s (exact causal pairs x 2 GEMMs x 2) against the bf16
+    tensor peak and, for the mixed batch, the combined bound B/BW + F/peak.
+    """
+    import torch
+
+    import microinfer_b200 as mi
+    from oracle.paged_oracle import prefill_flops
+
+    g = torch.Generator(device=device).manual_seed(11)
+    b = _prefill_batch(workload, device, g)
+    pool = mi.KVCache(layers, b["nb"], BS, HKV, D, dtype=torch.bfloat16, device=device)
+    pool.keys.normal_(generator=g).mul_(0.5)
+    pool.values.normal_(generator=g).mul_(0.5)
+    tokens = int(sum(b["q_lens"]))
+    q = torch.randn(tokens, HQ, D, generator=g, device=device).to(torch.bfloat16)
+    kn = torch.randn(tokens, HKV, D, generator=g, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    views = [pool.layer(i) for i in range(layers)]
+    max_q = max(b["q_lens"])
+
+    def run():
+        for view in views:
+            view.write_slots(b["slots"], kn, kn)
+            mi.paged_prefill(q, view.keys, view.values, b["cu_q"], b["cu_k"], b["table"],
+                             max_seqlen_q=max_q, out=out)
+
+    run()
+    torch.cuda.synchronize(device)
+    mi.check_device_status(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run()
+    graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms_layer = e0.elapsed_time(e1) / reps / layers
+    flops = prefill_flops(b["q_lens"], b["contexts"], HQ, D)
+    kv_bytes = sum(2 * c * HKV * D * 2 for c in b["contexts"])
+    if workload == "prefix":  # the shared prefix is stored once
+        kv_bytes = 2 * (1024 + 64 * 128) * HKV * D * 2
+    peaks, src = _peaks()
+    tflops = flops / (ms_layer * 1e-3) / 1e12
+    res = {"workload": ("BASELINE configs[2]: 24 decode + 8x512 prefill chunks, one launch"
+                        if workload == "mixed" else
+                        "BASELINE configs[3]: 64 x 128-token suffix on a shared 1024 prefix"),
+           "kernel": "prefill_tc_kernel (tcgen05)", "layers": layers,
+           "us_per_layer": round(ms_layer * 1e3, 2), "flops_per_layer": flops,
+           "tflops": round(tflops, 1), "tensor_frac": round(tflops / peaks["bf16_tflops"], 4),
+           "peak_source": f"bf16_tflops of {src}", "store_tokens": tokens}
+    if workload == "mixed":
+        t_min = kv_bytes / (peaks["hbm_gbs"] * 1e9) + flops / (peaks["bf16_tflops"] * 1e12)
+        res["combined_bound_frac"] = round(t_min / (ms_layer * 1e-3), 4)
+        res["kv_bytes_per_layer"] = kv_bytes
+    del graph, pool
+    return res
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -286,8 +396,10 @@ def run_ours(args):
     def attention_layers():
         # store_kvcache fused into paged decode: one launch per layer
         for i, view in enumerate(views):
+            # Layer i+1's launch only follows layer i's decode, which writes neither
+            # layer i+1's pool nor the tables: its pages may load early (PDL).
             mi.paged_decode_store(q[i], view.keys, view.values, table_d, ctx_d, kn[i], vn[i],
-                                  slots_d, split_k=split, out=out[i])
+                                  slots_d, split_k=split, out=out[i], early_kv=True)
 
     def layer_loop():
         attention_layers()
@@ -445,7 +557,9 @@ def run_ours(args):
             "clocks": clocks.summary(),
         }
         if world == 1:
-            line["extra"] = {"long_context_b1": measure_long_b1(device)}
+            line["extra"] = {"long_context_b1": measure_long_b1(device),
+                             "prefill_mixed": measure_prefill(device, "mixed"),
+                             "prefill_shared_prefix": measure_prefill(device, "prefix")}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
@@ -467,6 +581,28 @@ def run_profile(args):
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
+    if args.profile in ("prefill", "mixed"):
+        workload = "prefix" if args.profile == "prefill" else "mixed"
+        g = torch.Generator(device=device).manual_seed(11)
+        b = _prefill_batch(workload, device, g)
+        layers = 2
+        pool = mi.KVCache(layers, b["nb"], BS, HKV, D, dtype=torch.bfloat16, device=device)
+        pool.keys.normal_(generator=g).mul_(0.5)
+        pool.values.normal_(generator=g).mul_(0.5)
+        tokens = int(sum(b["q_lens"]))
+        q = torch.randn(tokens, HQ, D, generator=g, device=device).to(torch.bfloat16)
+        for _ in range(args.steps):
+            for i in range(layers):
+                view = pool.layer(i)
+                mi.paged_prefill(q, view.keys, view.values, b["cu_q"], b["cu_k"], b["table"],
+                                 max_seqlen_q=max(b["q_lens"]))
+        torch.cuda.synchronize(device)
+        mi.check_device_status(device)
+        from oracle.paged_oracle import prefill_flops
+
+        print(json.dumps({"profile": args.profile, "layers": layers, "iterations": args.steps,
+                          "flops_per_launch": prefill_flops(b["q_lens"], b["contexts"], HQ, D)}))
+        return
     layers = 4
     ctx, table, slots = make_batch(1000, device)
     ctx_d, table_d, slots_d = ctx.to(device), table.to(device), slots.to(device)
@@ -496,7 +632,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["decode"], default=None,
+    ap.add_argument("--profile", choices=["decode", "prefill", "mixed"], default=None,
                     help="run a small eager case for ncu instead of the benchmark")
     ap.add_argument("--split-k", type=int, default=0)
     args = ap.parse_args()

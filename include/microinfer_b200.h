@@ -158,7 +158,15 @@ MI_API int mi_paged_decode_uses_workspace(int32_t num_splits);
  * microinfer/runner.py:160-177).  Replaces the LayerKVCache.write_fast +
  * paged_attention_meta pair of CachedAttention.forward for decode
  * (microinfer/layer/cached_attention.py:76-85) with one launch.
+ *
+ * flags: MI_DECODE_EARLY_KV lets the kernel read the block table, context
+ * lengths and cached pages before it waits on the preceding kernel in the
+ * stream (programmatic dependent launch), so page loads overlap that
+ * kernel's tail; only query and k_new/v_new are taken to be produced by it.
+ * Set it only when the preceding kernel does not write the pool, the tables
+ * or the lengths (e.g. a QKV projection, or the previous layer's decode).
  */
+#define MI_DECODE_EARLY_KV 1
 MI_API int mi_paged_decode_store(void *out, const void *query, void *key_cache,
                           void *value_cache, int64_t num_blocks,
                           int32_t block_size, int32_t num_q_heads,
@@ -169,9 +177,9 @@ MI_API int mi_paged_decode_store(void *out, const void *query, void *key_cache,
                           const void *k_new, const void *v_new,
                           int64_t new_token_stride,
                           const int32_t *slot_mapping, float scale,
-                          int32_t num_splits, void *workspace,
-                          size_t workspace_bytes, int32_t *dev_status,
-                          void *stream);
+                          int32_t num_splits, int32_t flags,
+                          void *workspace, size_t workspace_bytes,
+                          int32_t *dev_status, void *stream);
 
 /*
  * Allocation-free paged decode.  No counterpart in the reference: it exists
@@ -215,6 +223,16 @@ MI_API int mi_paged_prefill(void *out, const void *query, const void *key_cache,
                      const int32_t *block_tables, int64_t block_table_stride,
                      int64_t num_seqs, int64_t num_tokens, int32_t max_seqlen_q,
                      float scale, int32_t *dev_status, void *stream);
+
+/*
+ * Which kernel mi_paged_prefill / mi_varlen_prefill dispatch to for a shape
+ * with 16-byte aligned tensors: 2 = tcgen05 tensor-core kernel, 1 = generic
+ * CUDA-core kernel, negative = invalid shape.  block_size 0 asks for the
+ * dense (varlen) mode.
+ */
+MI_API int mi_prefill_kernel_for(int32_t dtype, int32_t head_dim,
+                          int32_t num_q_heads, int32_t num_kv_heads,
+                          int32_t block_size);
 
 /*
  * Dense varlen causal prefill on this step's contiguous K/V (no cached

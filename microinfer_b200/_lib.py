@@ -53,13 +53,14 @@ SIGNATURES = {
     "mi_paged_decode_store": (
         ctypes.c_int,
         [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _P, _P, _I64, _P,
-         _F, _I32, _P, _SZ, _P, _P],
+         _F, _I32, _I32, _P, _SZ, _P, _P],
     ),
     "mi_paged_decode_noalloc": (
         ctypes.c_int,
         [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _F, _I32, _P,
          _P],
     ),
+    "mi_prefill_kernel_for": (ctypes.c_int, [_I32, _I32, _I32, _I32, _I32]),
     "mi_paged_prefill": (
         ctypes.c_int,
         [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _P, _P, _I64, _I64, _I64, _I32,

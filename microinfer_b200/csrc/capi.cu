@@ -243,7 +243,7 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
                 int64_t num_blocks, int32_t block_size, int32_t num_q_heads, int32_t num_kv_heads,
                 int32_t head_dim, int32_t dtype, const int32_t *block_tables,
                 int64_t block_table_stride, const int32_t *context_lens, int64_t num_seqs,
-                const NewToken *nt, float scale, int32_t num_splits, void *workspace,
+                const NewToken *nt, float scale, int32_t num_splits, int32_t flags, void *workspace,
                 size_t workspace_bytes, int32_t *dev_status, void *stream) {
   const int e = elem_size(dtype);
   if (e == 0) return fail(MI_ERR_INVALID, "unknown dtype");
@@ -351,6 +351,9 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
   } else if (nsplit > 1) {
     p.cluster_combine = 1;
   }
+  if (flags & MI_DECODE_EARLY_KV) {
+    p.early_kv = 1;
+  }
   return cuda_status(launch_decode_fast(p, dtype, head_dim, G, num_seqs, nsplit, st));
 }
 
@@ -370,7 +373,7 @@ int mi_paged_decode(void *out, const void *query, const void *key_cache, const v
                     void *workspace, size_t workspace_bytes, int32_t *dev_status, void *stream) {
   return decode_impl(out, query, key_cache, value_cache, num_blocks, block_size, num_q_heads,
                      num_kv_heads, head_dim, dtype, block_tables, block_table_stride, context_lens,
-                     num_seqs, nullptr, scale, num_splits, workspace, workspace_bytes, dev_status,
+                     num_seqs, nullptr, scale, num_splits, 0, workspace, workspace_bytes, dev_status,
                      stream);
 }
 
@@ -381,12 +384,13 @@ int mi_paged_decode_store(void *out, const void *query, void *key_cache, void *v
                           const int32_t *context_lens, int64_t num_seqs, const void *k_new,
                           const void *v_new, int64_t new_token_stride,
                           const int32_t *slot_mapping, float scale, int32_t num_splits,
-                          void *workspace, size_t workspace_bytes, int32_t *dev_status,
-                          void *stream) {
+                          int32_t flags, void *workspace, size_t workspace_bytes,
+                          int32_t *dev_status, void *stream) {
+  if (flags & ~MI_DECODE_EARLY_KV) return fail(MI_ERR_INVALID, "unknown decode flags");
   const NewToken nt{k_new, v_new, new_token_stride, slot_mapping};
   return decode_impl(out, query, key_cache, value_cache, num_blocks, block_size, num_q_heads,
                      num_kv_heads, head_dim, dtype, block_tables, block_table_stride, context_lens,
-                     num_seqs, &nt, scale, num_splits, workspace, workspace_bytes, dev_status,
+                     num_seqs, &nt, scale, num_splits, flags, workspace, workspace_bytes, dev_status,
                      stream);
 }
 
@@ -439,8 +443,20 @@ static int prefill_common(void *out, const void *query, const void *kbase, const
   const bool tc = prefill_tc_supported(dtype, head_dim, G, paged ? block_size : 16) &&
                   aligned16(kbase) && aligned16(vbase) && aligned16(query) && aligned16(out) &&
                   (paged || (kv_token_stride * e) % 16 == 0);
-  if (tc) return cuda_status(launch_prefill_tc(p, dtype, G, max_seqlen_q, paged, st));
+  if (tc) {
+    const cudaError_t te = launch_prefill_tc(p, dtype, G, max_seqlen_q, paged, st);
+    if (te != cudaErrorNotSupported) return cuda_status(te);  // else: shape outside its grid limits
+  }
   return cuda_status(launch_attn_generic(p, dtype, paged, st));
+}
+
+int mi_prefill_kernel_for(int32_t dtype, int32_t head_dim, int32_t num_q_heads,
+                          int32_t num_kv_heads, int32_t block_size) {
+  if (elem_size(dtype) == 0 || head_dim <= 0 || head_dim > 256 || num_q_heads <= 0 ||
+      num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0 || block_size < 0)
+    return fail(MI_ERR_INVALID, "invalid shape");
+  const int G = num_q_heads / num_kv_heads;
+  return prefill_tc_supported(dtype, head_dim, G, block_size == 0 ? 16 : block_size) ? 2 : 1;
 }
 
 int mi_paged_prefill(void *out, const void *query, const void *key_cache, const void *value_cache,

@@ -126,7 +126,8 @@ __global__ void __launch_bounds__(256, G >= 8 ? 1 : 2) paged_decode_kernel(Decod
   }
   __syncwarp();
 
-  pdl_wait();
+  // Without early_kv everything below may come from the preceding kernel.
+  if (!p.early_kv) pdl_wait();
   // ---- one round trip: context, first table entries, this step's slot ----
   const int32_t *table = p.block_tables + seq * p.bt_stride;
   auto chunk_of = [&](int it) { return split + nsplit * (warp + C::kWarps * it); };
@@ -203,14 +204,31 @@ __global__ void __launch_bounds__(256, G >= 8 ? 1 : 2) paged_decode_kernel(Decod
     }
   };
 
-  // Prologue: fill the ring.
+  // Prologue: fill the ring.  With early_kv the cached pages are requested
+  // before waiting on the preceding kernel; the chunk that receives this
+  // step's token (whose K/V that kernel may have produced) waits for it.
   int issued = 0;
+  int deferred = -1;
+  int64_t deferred_blk = -1;
 #pragma unroll
   for (int s = 0; s < C::kStages; ++s) {
     if (s < my_n) {
       const int ci = chunk_of(s);
-      issue(ci, s, check_blk(ci, pre_blk[s]));
+      if (p.early_kv && own_last && ci == last_chunk) {
+        deferred = s;
+        deferred_blk = pre_blk[s];
+      } else {
+        issue(ci, s, check_blk(ci, pre_blk[s]));
+      }
       ++issued;
+    }
+  }
+  if (p.early_kv) {
+    pdl_launch_dependents();  // the next kernel may start its own prologue
+    pdl_wait();
+    if (deferred >= 0) {
+      const int ci = chunk_of(deferred);
+      issue(ci, deferred, check_blk(ci, deferred_blk));
     }
   }
 

@@ -91,6 +91,12 @@ struct DecodeParams {
   // 1: the splits of one (seq, kv head) form a thread-block cluster and are
   // merged through distributed shared memory (no workspace, no combine launch).
   int32_t cluster_combine;
+  // 1: read the block table, context lengths and cached pages before waiting
+  // on the preceding kernel (programmatic dependent launch), so this layer's
+  // page loads overlap the previous kernel's tail.  Only q and this step's
+  // token are treated as produced by the preceding kernel; the caller
+  // guarantees that kernel does not write the pool, tables or lengths.
+  int32_t early_kv;
 };
 
 }  // namespace mi

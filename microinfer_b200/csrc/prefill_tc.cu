@@ -1,27 +1,515 @@
 // tcgen05 (UMMA + TMEM) paged chunked-prefill attention for sm_100a.
+//
+// Work tile: 128 query rows = (TQ = 128/G tokens) x (G query heads of one kv
+// head), against every cached key of the sequence up to the tile's last
+// position, in 128-key tiles.  One CTA per (query tile, kv head, sequence);
+// 192 threads in three roles:
+//
+//   warp 0      TMA producer: Q once (two 64-column halves, 3-D map over
+//               [tokens, Hq, D]), then per key tile 8 groups of 16 keys for
+//               K and for V (3-D map over [slots, Hkv, D]); each group's slot
+//               comes from the block table, groups past the context load from
+//               an out-of-range coordinate (zero fill).  K/V ring of 2 stages.
+//   warp 1      TMEM owner and single-thread MMA issuer:
+//                 S[j%2] = Q K_j^T   (M=128, N=128, K=D; A, B K-major)
+//                 O     += P_j V_j   (M=128, N=D,   K=128; B MN-major)
+//               S is double-buffered so S_{j+1} overlaps the softmax of S_j.
+//   warps 2-5   softmax: one TMEM lane (= query row) per thread; read S with
+//               tcgen05.ld, causal mask (key <= row position), online softmax
+//               in the log2 domain with lazy rescale of O (only when the row
+//               max grows by more than 2^8), write P as fp16/bf16 into the
+//               128-byte-swizzled shared tile the next MMA reads; epilogue
+//               O / l -> global.
+//
+// Shared memory operands use the SWIZZLE_128B canonical layout (8 rows x 128
+// bytes atoms); a 128x128 16-bit tile is two 16 KB column halves.  TMEM: S0
+// at column 0, S1 at 128, O at 256 (512 columns allocated).
+//
+// Dense mode (no block table) reads K/V rows cu_seqlens_k[s] + key of a
+// contiguous [tokens, Hkv, D] tensor: the no-prefix ("direct") prefill.
+// Every mbarrier wait is bounded; a timeout flags MI_DEV_TIMEOUT, unwinds,
+// waits for this CTA's own copies and MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "launch.cuh"
 #include "params.cuh"
+#include "tc_helpers.cuh"
 
 namespace mi {
 
-bool prefill_tc_supported(int dtype, int D, int G, int block_size) {
-  (void)dtype;
-  (void)D;
-  (void)G;
-  (void)block_size;
-  return false;
+struct __align__(64) PrefillTcParams {
+  CUtensorMap tmap_q;
+  CUtensorMap tmap_k;
+  CUtensorMap tmap_v;
+  void *out;
+  const int32_t *cu_q;
+  const int32_t *cu_k;
+  const int32_t *block_tables;
+  int64_t bt_stride;
+  int64_t num_blocks;
+  int64_t kv_rows;  // extent of the K/V maps' row dimension (OOB coordinate)
+  int32_t block_size;
+  int32_t num_q_heads;
+  int32_t paged;
+  float scale_log2;
+  int32_t *status;
+};
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int kTileBytes = 32768;  // 128 x 128 x 16-bit
+constexpr int kHalf = 16384;
+constexpr int kOffQ = 0;
+constexpr int kOffK = kOffQ + kTileBytes;      // 2 stages
+constexpr int kOffV = kOffK + 2 * kTileBytes;  // 2 stages
+constexpr int kOffP = kOffV + 2 * kTileBytes;
+constexpr int kOffBar = kOffP + kTileBytes;
+constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + TMEM slot + alignment slack
+constexpr uint32_t kTmemCols = 512;
+
+// barrier indices
+enum {
+  B_Q = 0,
+  B_KFULL = 1,   // +stage
+  B_VFULL = 3,   // +stage
+  B_KEMPTY = 5,  // +stage
+  B_VEMPTY = 7,  // +stage
+  B_SFULL = 9,   // +buffer
+  B_SEMPTY = 11, // +buffer
+  B_PFULL = 13,
+  B_ODONE = 14,
+  B_FIN = 15,
+  B_COUNT = 16
+};
+
+// K-major SW128 descriptor of 16-element K-step `kk` of a 128 x 128 tile.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, int kk) {
+  return tc::smem_desc_sw128(tile + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+}
+// MN-major SW128 descriptor (V as the B operand): K-step kk = 16 key rows.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile, int kk) {
+  return tc::smem_desc_sw128(tile + kk * 2048, kHalf, 1024);
 }
 
-cudaError_t launch_prefill_tc(const AttnParams &p, int dtype, int G, int32_t max_seqlen_q,
-                              bool paged, cudaStream_t stream) {
-  (void)p;
-  (void)dtype;
-  (void)G;
-  (void)max_seqlen_q;
-  (void)paged;
-  (void)stream;
-  return cudaErrorNotSupported;
+__device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
+  if (bf16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+  }
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+}  // namespace
+
+template <typename T, int G>
+__global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ PrefillTcParams p) {
+  constexpr int TQ = 128 / G;  // tokens per tile
+  constexpr bool kBf16 = sizeof(T) == 2 && Elem<T>::kDtype == MI_DTYPE_BFLOAT16;
+  constexpr uint32_t kIdescQK = tc::idesc_f16(128, 128, kBf16 ? 1 : 0, false);
+  constexpr uint32_t kIdescPV = tc::idesc_f16(128, 128, kBf16 ? 1 : 0, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kOffBar);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + B_COUNT);
+  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+  const uint32_t sQ = smem_addr(smem + kOffQ);
+  const uint32_t sK = smem_addr(smem + kOffK);
+  const uint32_t sV = smem_addr(smem + kOffV);
+  const uint32_t sP = smem_addr(smem + kOffP);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, kvh = blockIdx.y;
+  const int64_t seq = blockIdx.z;
+
+  pdl_wait();
+  const int q_start = p.cu_q[seq];
+  const int q_len = p.cu_q[seq + 1] - q_start;
+  const int t0 = qt * TQ;
+  if (t0 >= q_len) return;  // uniform: this sequence has fewer query tiles
+  const int kv0 = p.cu_k[seq];
+  const int ctx = p.cu_k[seq + 1] - kv0;
+  const int prefix = ctx - q_len;
+  const int nt = min(TQ, q_len - t0);
+  const int maxpos = prefix + t0 + nt - 1;
+  const int nkv = maxpos >= 0 ? maxpos / 128 + 1 : 0;
+  T *out = static_cast<T *>(p.out);
+  if (nkv == 0) {  // no visible key (context shorter than the chunk): zeros, as the generic kernel
+    for (int i = threadIdx.x; i < nt * G * 128; i += kThreads) {
+      const int row = i / 128, d = i % 128;
+      out[(static_cast<int64_t>(q_start + t0 + row / G) * p.num_q_heads + kvh * G + row % G) * 128 + d] =
+          Elem<T>::from_float(0.f);
+    }
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[B_Q], 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar[B_KFULL + s], 1);
+      mbar_init(&bar[B_VFULL + s], 1);
+      mbar_init(&bar[B_KEMPTY + s], 1);
+      mbar_init(&bar[B_VEMPTY + s], 1);
+      mbar_init(&bar[B_SFULL + s], 1);
+      mbar_init(&bar[B_SEMPTY + s], 128);
+    }
+    mbar_init(&bar[B_PFULL], 128);
+    mbar_init(&bar[B_ODONE], 1);
+    mbar_init(&bar[B_FIN], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, kTmemCols);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 256;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    const int32_t *table = p.block_tables + seq * p.bt_stride;
+    auto kv_row = [&](int key0) -> int {
+      if (key0 >= ctx) return static_cast<int>(p.kv_rows);  // past the context: zero fill
+      if (!p.paged) return kv0 + key0;
+      const int64_t col = key0 / p.block_size;
+      const int64_t blk = col < p.bt_stride ? table[col] : -1;
+      if (blk < 0 || blk >= p.num_blocks) {
+        flag_status(p.status, MI_DEV_BAD_BLOCK);
+        return static_cast<int>(p.kv_rows);
+      }
+      return static_cast<int>(blk * p.block_size + key0 % p.block_size);
+    };
+    bool ok = true;
+    int kv_armed = 0;  // key tiles whose loads were issued
+    if (lane == 0) {
+      tc::prefetch_tmap(&p.tmap_q);
+      tc::prefetch_tmap(&p.tmap_k);
+      tc::prefetch_tmap(&p.tmap_v);
+      mbar_arrive_expect_tx(&bar[B_Q], 2 * kHalf);
+      for (int dh = 0; dh < 2; ++dh)
+        tc::tma_load_3d(smem + kOffQ + dh * kHalf, &p.tmap_q, dh * 64, kvh * G, q_start + t0, &bar[B_Q]);
+    }
+    for (int j = 0; j < nkv && ok; ++j) {
+      const int s = j & 1;
+      const uint32_t empty_parity = ((j >> 1) & 1) ^ 1;
+      // lanes 0..15 each load one (16-key group, 64-column half) box
+      const int g = lane >> 1, dh = lane & 1;
+      const int row = lane < 16 ? kv_row(j * 128 + g * 16) : 0;
+      for (int kv = 0; kv < 2 && ok; ++kv) {
+        uint64_t *empty = &bar[(kv ? B_VEMPTY : B_KEMPTY) + s];
+        uint64_t *full = &bar[(kv ? B_VFULL : B_KFULL) + s];
+        int good = 1;
+        if (lane == 0) good = mbar_wait_bounded(empty, empty_parity, p.status) && !*(volatile int *)abort_flag;
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) mbar_arrive_expect_tx(full, kTileBytes);
+        __syncwarp();
+        if (lane < 16)
+          tc::tma_load_3d(smem + (kv ? kOffV : kOffK) + s * kTileBytes + dh * kHalf + g * 2048,
+                          kv ? &p.tmap_v : &p.tmap_k, dh * 64, kvh, row, full);
+      }
+      if (ok) kv_armed = j + 1;
+    }
+    if (!ok) {
+      if (lane == 0) *(volatile int *)abort_flag = 1;
+      // Let this CTA's own loads in flight land before its shared memory goes away.
+      if (lane == 0)
+        for (int j = max(0, kv_armed - 2); j < kv_armed; ++j) {
+          mbar_wait_bounded(&bar[B_KFULL + (j & 1)], (j >> 1) & 1, p.status);
+          mbar_wait_bounded(&bar[B_VFULL + (j & 1)], (j >> 1) & 1, p.status);
+        }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait_bounded(&bar[B_Q], 0, p.status);
+      auto pv = [&](int jj) -> bool {
+        const int s = jj & 1;
+        if (!mbar_wait_bounded(&bar[B_PFULL], jj & 1, p.status)) return false;
+        if (!mbar_wait_bounded(&bar[B_VFULL + s], (jj >> 1) & 1, p.status)) return false;
+        tc::fence_after_sync();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc::umma_f16(tO, kmajor_desc(sP, kk), mnmajor_desc(sV + s * kTileBytes, kk), kIdescPV,
+                       (jj > 0 || kk > 0) ? 1u : 0u);
+        tc::umma_commit(&bar[B_ODONE]);
+        tc::umma_commit(&bar[B_VEMPTY + s]);
+        return true;
+      };
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int s = j & 1;
+        ok = mbar_wait_bounded(&bar[B_KFULL + s], (j >> 1) & 1, p.status) &&
+             mbar_wait_bounded(&bar[B_SEMPTY + s], ((j >> 1) & 1) ^ 1, p.status) &&
+             !*(volatile int *)abort_flag;
+        if (!ok) break;
+        tc::fence_after_sync();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc::umma_f16(tS + s * 128, kmajor_desc(sQ, kk), kmajor_desc(sK + s * kTileBytes, kk),
+                       kIdescQK, kk > 0 ? 1u : 0u);
+        tc::umma_commit(&bar[B_SFULL + s]);
+        tc::umma_commit(&bar[B_KEMPTY + s]);
+        if (j >= 1) ok = pv(j - 1);
+      }
+      if (ok) ok = pv(nkv - 1);
+      if (!ok) *(volatile int *)abort_flag = 1;
+      // Every MMA issued by this thread completes before TMEM is released.
+      tc::umma_commit(&bar[B_FIN]);
+      mbar_wait_bounded(&bar[B_FIN], 0, p.status);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;  // TMEM lane = query row of the tile
+    const int tok = r / G;
+    const bool rvalid = tok < nt;
+    const int pos = prefix + t0 + tok;
+    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    uint8_t *prow = smem + kOffP + r * 128;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int s = j & 1;
+      int good = mbar_wait_bounded(&bar[B_SFULL + s], (j >> 1) & 1, p.status) &&
+                 !*(volatile int *)abort_flag;
+      if (!__all_sync(0xffffffffu, good)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      float x[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tc::tmem_ld32(tS + s * 128 + lane_off + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[c * 32 + i] = v[i];
+      }
+      tc::tmem_wait_ld();
+      tc::fence_before_sync();
+      mbar_arrive(&bar[B_SEMPTY + s]);
+
+      const int lim = rvalid ? pos - j * 128 : -1;  // key c of this tile visible iff c <= lim
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        x[c] = c <= lim ? x[c] * p.scale_log2 : -INFINITY;
+        mx = fmaxf(mx, x[c]);
+      }
+      float m_new = m, alpha = 1.f;
+      bool rescale = false;
+      if (mx > m + 8.f) {
+        m_new = mx;
+        rescale = m != -INFINITY;
+        alpha = rescale ? fast_exp2(m - m_new) : 0.f;
+      }
+      // P_{j-1} must be consumed (and O settled) before P_j / O are touched.
+      if (j >= 1) {
+        good = mbar_wait_bounded(&bar[B_ODONE], (j - 1) & 1, p.status);
+        if (!__all_sync(0xffffffffu, good)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        if (__any_sync(0xffffffffu, rescale)) {
+          const float a = rescale ? alpha : 1.f;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tc::tmem_ld32(tO + lane_off + c * 32, o);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= a;
+            tc::tmem_st32(tO + lane_off + c * 32, o);
+          }
+          tc::tmem_wait_st();
+        }
+      }
+      float rs = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float xv = x[c8 * 8 + i];
+          e[i] = xv == -INFINITY ? 0.f : fast_exp2(xv - m_new);
+          rs += e[i];
+        }
+        uint4 w;
+        w.x = pack2(e[0], e[1], kBf16);
+        w.y = pack2(e[2], e[3], kBf16);
+        w.z = pack2(e[4], e[5], kBf16);
+        w.w = pack2(e[6], e[7], kBf16);
+        const int half = c8 >> 3, chunk = c8 & 7;
+        *reinterpret_cast<uint4 *>(prow + half * kHalf + ((chunk ^ (r & 7)) << 4)) = w;
+      }
+      l = l * alpha + rs;
+      m = m_new;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
+      tc::fence_before_sync();
+      mbar_arrive(&bar[B_PFULL]);
+    }
+    if (ok) {
+      const int good = mbar_wait_bounded(&bar[B_ODONE], (nkv - 1) & 1, p.status);
+      ok = __all_sync(0xffffffffu, good);
+    }
+    if (ok) {
+      tc::fence_after_sync();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T *orow = out + (static_cast<int64_t>(q_start + t0 + tok) * p.num_q_heads + kvh * G + r % G) * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        tc::tmem_ld32(tO + lane_off + c * 32, o);
+        tc::tmem_wait_ld();
+        if (rvalid) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            w.x = pack2(o[i] * inv, o[i + 1] * inv, kBf16);
+            w.y = pack2(o[i + 2] * inv, o[i + 3] * inv, kBf16);
+            w.z = pack2(o[i + 4] * inv, o[i + 5] * inv, kBf16);
+            w.w = pack2(o[i + 6] * inv, o[i + 7] * inv, kBf16);
+            *reinterpret_cast<uint4 *>(orow + c * 32 + i) = w;
+          }
+        }
+      }
+    } else if (lane == 0) {
+      *(volatile int *)abort_flag = 1;
+    }
+  }
+
+  pdl_launch_dependents();
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 3-D map (x = D columns, y = heads, z = rows) with a {64, box_y, box_z} box.
+bool encode_3d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t d, uint64_t heads,
+               uint64_t rows, uint64_t head_stride_bytes, uint64_t row_stride_bytes, uint32_t box_y,
+               uint32_t box_z) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {d, heads, rows};
+  cuuint64_t strides[2] = {head_stride_bytes, row_stride_bytes};
+  cuuint32_t box[3] = {64, box_y, box_z};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, dt, 3, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T, int G>
+cudaError_t launch_tg(PrefillTcParams &p, int num_kv_heads, int64_t num_seqs, int32_t max_seqlen_q,
+                      cudaStream_t stream) {
+  auto kern = prefill_tc_kernel<T, G>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  constexpr int TQ = 128 / G;
+  const dim3 grid((max_seqlen_q + TQ - 1) / TQ, num_kv_heads, static_cast<unsigned>(num_seqs));
+  return launch_pdl(kern, grid, dim3(kThreads), kSmemBytes, stream, p);
+}
+
+}  // namespace
+
+bool prefill_tc_supported(int dtype, int D, int G, int block_size) {
+  if (dtype != MI_DTYPE_BFLOAT16 && dtype != MI_DTYPE_FLOAT16) return false;
+  if (D != 128) return false;
+  if (G != 1 && G != 2 && G != 4 && G != 8) return false;
+  if (block_size < 16 || block_size % 16 != 0) return false;
+  return encode_fn() != nullptr;
+}
+
+cudaError_t launch_prefill_tc(const AttnParams &a, int dtype, int G, int32_t max_seqlen_q, bool paged,
+                              cudaStream_t stream) {
+  if (a.num_seqs > 65535 || a.num_kv_heads > 65535) return cudaErrorNotSupported;
+  const int e = 2;
+  const CUtensorMapDataType dt =
+      dtype == MI_DTYPE_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uint64_t D = 128;
+  PrefillTcParams p;
+  memset(&p, 0, sizeof(p));
+  const uint32_t TQ = 128 / G;
+  if (!encode_3d(&p.tmap_q, dt, a.query, D, a.num_q_heads, a.num_tokens, D * e,
+                 static_cast<uint64_t>(a.num_q_heads) * D * e, G, TQ))
+    return cudaErrorInvalidValue;
+  uint64_t rows, row_stride;
+  if (paged) {
+    rows = static_cast<uint64_t>(a.num_blocks) * a.block_size;
+    row_stride = static_cast<uint64_t>(a.num_kv_heads) * D * e;
+  } else {
+    rows = static_cast<uint64_t>(a.kv_rows);
+    row_stride = static_cast<uint64_t>(a.kv_token_stride) * e;
+  }
+  if (rows == 0 || rows >= (1ull << 31)) return cudaErrorNotSupported;
+  if (!encode_3d(&p.tmap_k, dt, a.key_base, D, a.num_kv_heads, rows, D * e, row_stride, 1, 16) ||
+      !encode_3d(&p.tmap_v, dt, a.value_base, D, a.num_kv_heads, rows, D * e, row_stride, 1, 16))
+    return cudaErrorInvalidValue;
+  p.out = a.out;
+  p.cu_q = a.cu_q;
+  p.cu_k = a.cu_k;
+  p.block_tables = a.block_tables;
+  p.bt_stride = a.bt_stride;
+  p.num_blocks = a.num_blocks;
+  p.kv_rows = static_cast<int64_t>(rows);
+  p.block_size = paged ? a.block_size : 16;
+  p.num_q_heads = a.num_q_heads;
+  p.paged = paged ? 1 : 0;
+  p.scale_log2 = a.scale_log2;
+  p.status = a.status;
+  const int64_t n = a.num_seqs;
+  if (dtype == MI_DTYPE_BFLOAT16) {
+    switch (G) {
+      case 1: return launch_tg<__nv_bfloat16, 1>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+      case 2: return launch_tg<__nv_bfloat16, 2>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+      case 4: return launch_tg<__nv_bfloat16, 4>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+      default: return launch_tg<__nv_bfloat16, 8>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+    }
+  }
+  switch (G) {
+    case 1: return launch_tg<__half, 1>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+    case 2: return launch_tg<__half, 2>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+    case 4: return launch_tg<__half, 4>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+    default: return launch_tg<__half, 8>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+  }
 }
 
 }  // namespace mi

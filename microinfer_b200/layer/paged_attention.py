@@ -115,12 +115,17 @@ def paged_decode(query, key_cache, value_cache, block_tables, context_lens, *,
 
 def paged_decode_store(query, key_cache, value_cache, block_tables, context_lens, k_new, v_new,
                        slot_mapping, *, scale: float | None = None, split_k: int | None = None,
-                       out: torch.Tensor | None = None) -> torch.Tensor:
+                       out: torch.Tensor | None = None, early_kv: bool = False) -> torch.Tensor:
     """store_kvcache of this step's token fused into paged decode (one launch).
 
     ``k_new``/``v_new`` are ``[requests, Hkv, D]`` (inner dims contiguous);
     ``slot_mapping[r]`` (-1 = padding) must address position
     ``context_lens[r] - 1`` of request r, as the reference runner builds it.
+
+    ``early_kv=True`` lets the launch request its cached pages before the
+    preceding kernel in the stream has finished (programmatic dependent
+    launch); use it only when that kernel writes neither the pool nor the
+    tables/lengths (a QKV projection, or another layer's decode).
     """
     if query.shape[0] == 0:
         return torch.empty_like(query)
@@ -144,7 +149,8 @@ def paged_decode_store(query, key_cache, value_cache, block_tables, context_lens
         value_cache.data_ptr(), *a["dims"], a["block_tables"].data_ptr(),
         a["block_tables"].stride(0), a["context_lens"].data_ptr(), n, k_new.data_ptr(),
         v_new.data_ptr(), k_new.stride(0), slots.data_ptr(), a["scale"], a["split_k"],
-        _lib.ptr(a["workspace"]), a["ws_bytes"], _lib.status_buffer(a["device"]).data_ptr(),
+        1 if early_kv else 0, _lib.ptr(a["workspace"]), a["ws_bytes"],
+        _lib.status_buffer(a["device"]).data_ptr(),
         _lib.stream_of(a["device"]),
     )
     return a["out"]

@@ -203,6 +203,24 @@ def build(name: str) -> dict:
             nxt += 2
         return prefill_case(44, [suffix] * n, [prefix + suffix] * n, 16, 8, 128, bs, 16, "bf16",
                             pool_scale=0.5, table=table)
+    if name.startswith("tc_prefill_g"):
+        # Tensor-core prefill shapes: D=128, 2 kv heads, chunks spanning several
+        # 128-row query tiles and 128-key tiles, prefixes off tile boundaries,
+        # plus a single-token (decode) row in the same launch.
+        g, dtype = name[len("tc_prefill_g"):].split("_")
+        g = int(g)
+        q_lens = [200, 37, 1, 129]
+        contexts = [200 + 200, 37 + 5, 1 + 130, 129]
+        return prefill_case(90 + g, q_lens, contexts, g, 1, 128, 16, 64, dtype, pool_scale=0.5)
+    if name.startswith("tc_prefill_bs"):
+        bs, dtype = name[len("tc_prefill_bs"):].split("_")
+        bs = int(bs)
+        q_lens = [150, 40]
+        contexts = [150 + 3 * bs + 7, 40 + 100]
+        nb = sum((c + bs - 1) // bs for c in contexts) + 2
+        return prefill_case(70 + bs, q_lens, contexts, 2, 1, 128, bs, nb, dtype, pool_scale=0.5)
+    if name == "tc_dense_g4_bf16":
+        return direct_case(57, [129, 64, 1, 100], 4, 1, 128, "bf16")
     if name == "direct_bf16":
         return direct_case(55, [5, 17, 33, 1], 16, 8, 128, "bf16")
     if name == "direct_f32":
@@ -217,18 +235,22 @@ def build(name: str) -> dict:
 DECODE_REF_CASES = [f"decode_bs{bs}_{dt}" for bs in (16, 32, 64, 128, 256)
                     for dt in ("f32", "f16", "bf16")]
 PREFILL_REF_CASES = [f"prefill_bs{bs}_{dt}" for bs in (16, 64) for dt in ("f16", "bf16")]
+TC_PREFILL_CASES = (["tc_prefill_g1_bf16", "tc_prefill_g2_bf16", "tc_prefill_g2_f16",
+                     "tc_prefill_g4_bf16", "tc_prefill_g4_f16", "tc_prefill_g8_bf16"]
+                    + [f"tc_prefill_bs{bs}_bf16" for bs in (32, 64, 128, 256)])
 CASES = (["cfg1_decode_f32", "cfg2_layer_bf16", "cfg5b_slice_bf16"] + DECODE_REF_CASES
          + PREFILL_REF_CASES + ["prefill_poison_bf16", "mixed_bf16", "prefix_bf16", "direct_bf16",
-                                "direct_f32", "cow_bf16", "write_checked_f32"])
+                                "direct_f32", "tc_dense_g4_bf16", "cow_bf16", "write_checked_f32"]
+         + TC_PREFILL_CASES)
 
 
 def kind(name: str) -> str:
     """Case kind without building its inputs."""
     if name.startswith(("cfg", "decode_")):
         return "decode"
-    if name.startswith(("prefill_", "mixed_", "prefix_")):
+    if name.startswith(("prefill_", "mixed_", "prefix_", "tc_prefill_")):
         return "prefill"
-    if name.startswith("direct_"):
+    if name.startswith(("direct_", "tc_dense_")):
         return "direct"
     if name.startswith("cow_"):
         return "cow"

@@ -58,7 +58,10 @@ def main(ref_root: str) -> None:
     from microinfer.worker.kv_cache import LayerKVCache
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+    force = "--force" in sys.argv
     for name in cases.CASES:
+        if (HERE / f"{name}.npz").exists() and not force:
+            continue  # fixtures are deterministic; keep committed bytes unchanged
         case = cases.build(name)
         dt = case["dtype"]
         out = {"digest_" + k: np.array(cases.digest(case[k])) for k in cases.INPUT_KEYS if k in case}
@@ -80,8 +83,9 @@ def main(ref_root: str) -> None:
             out["out"] = to_numpy(result, dt)
             slots = case["slots"].astype(np.int64)
             bs = case["block_size"]
-            out["stored_k"] = to_numpy(layer.keys[slots // bs, slots % bs], dt)
-            out["stored_v"] = to_numpy(layer.values[slots // bs, slots % bs], dt)
+            # stored rows are bit-exact: their digests pin them
+            out["stored_k_digest"] = np.array(cases.digest(to_numpy(layer.keys[slots // bs, slots % bs], dt)))
+            out["stored_v_digest"] = np.array(cases.digest(to_numpy(layer.values[slots // bs, slots % bs], dt)))
             gk, gv = _gather_paged_kv(layer.keys, layer.values, table, contexts, bs)
             out["gather_k_digest"] = np.array(cases.digest(to_numpy(gk, dt)))
             out["gather_v_digest"] = np.array(cases.digest(to_numpy(gv, dt)))
@@ -114,7 +118,8 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("MICROINFER_REFERENCE", "")
+    args = [a for a in sys.argv[1:] if not a.startswith("--")]
+    root = args[0] if args else os.environ.get("MICROINFER_REFERENCE", "")
     if not root:
         raise SystemExit("usage: make_golden.py /path/to/MicroInfer")
     main(root)

@@ -42,8 +42,8 @@ def test_oracle_matches_reference_store_attention_gather(name):
     kc, vc = _run_store(case)
     slots = case["slots"].astype(np.int64)
     bs = case["block_size"]
-    np.testing.assert_array_equal(kc[slots // bs, slots % bs], gold["stored_k"])
-    np.testing.assert_array_equal(vc[slots // bs, slots % bs], gold["stored_v"])
+    assert cases.digest(kc[slots // bs, slots % bs]) == str(gold["stored_k_digest"])
+    assert cases.digest(vc[slots // bs, slots % bs]) == str(gold["stored_v_digest"])
     if case["kind"] == "decode":
         cu_q = np.arange(len(case["contexts"]) + 1)
     else:
@@ -58,7 +58,7 @@ def test_oracle_matches_reference_store_attention_gather(name):
     assert cases.digest(gv) == str(gold["gather_v_digest"])
 
 
-@pytest.mark.parametrize("name", ["direct_bf16", "direct_f32"])
+@pytest.mark.parametrize("name", [c for c in cases.CASES if cases.kind(c) == "direct"])
 def test_oracle_matches_reference_direct_prefill(name):
     case = cases.build(name)
     gold = load_golden(name)
