@@ -191,7 +191,7 @@ def measure_long_b1(device, reps: int = 20):
     q = torch.randn(layers, 1, hq, D, generator=g, device=device).to(torch.bfloat16)
     kn = torch.randn(layers, 1, hkv, D, generator=g, device=device).to(torch.bfloat16)
     out = torch.empty_like(q)
-    split = mi.select_split_k(1, hkv, device)
+    kernel, split, _ = mi.decode_plan(1, hq, hkv, D, torch.bfloat16, BS, 0, device, nb)
     views = [pool.layer(i) for i in range(layers)]
 
     def run():
@@ -220,7 +220,8 @@ def measure_long_b1(device, reps: int = 20):
     peaks, src = _peaks()
     gbs = b / (ms * 1e-3) / 1e9
     return {"workload": "BASELINE configs[4] run (b): batch 1, context 32768, 32q/8kv, D128, "
-                        "36 layers, bs16", "split_k": split, "ms_per_step": round(ms, 4),
+                        "36 layers, bs16", "kernel": kernel, "split_k": split,
+            "ms_per_step": round(ms, 4),
             "value": round(gbs, 1), "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
             "peak_source": f"hbm_gbs of {src}", "tok_per_s": round(1000.0 / ms, 1)}
 
@@ -390,7 +391,8 @@ def run_ours(args):
     vn = torch.randn(LAYERS, NSEQ, HKV, D, generator=g, device=device).to(torch.bfloat16)
     out = torch.empty_like(q)
     tokens = torch.empty(NSEQ, dtype=torch.int32, device=device)
-    split = mi.select_split_k(NSEQ, HKV, device)
+    decode_kernel, split, _ = mi.decode_plan(NSEQ, HQ, HKV, D, torch.bfloat16, BS, 0, device,
+                                             table_d.shape[1])
     views = [pool.layer(i) for i in range(LAYERS)]
 
     def attention_layers():
@@ -535,14 +537,16 @@ def run_ours(args):
             "config": {"workload": WORKLOAD, "global_batch": NSEQ * world, "per_gpu_batch": NSEQ,
                        "context": [CTX_LO, CTX_HI], "layers": LAYERS, "block_size": BS,
                        "num_blocks_per_layer": NB, "heads": [HQ, HKV], "head_dim": D,
-                       "split_k": split, "parallelism": f"sequence-sharded x{world}",
+                       "split_k": split, "decode_kernel": decode_kernel,
+                       "parallelism": f"sequence-sharded x{world}",
                        "l2": "inputs larger than L2: 28 distinct layer pools, "
                              f"{step_bytes / 1e6:.0f} MB touched per step",
                        "graph": "28-layer store+decode CUDA graph replay"},
             "tok_per_s": round(world * NSEQ / (ms_step * 1e-3), 1),
             "median_step_ms": round(statistics.median(per_step), 5),
             "roofline": {"bound": "hbm",
-                         "kernel": "paged_decode_kernel (store fused, cluster split merge)",
+                         "kernel": ("paged_decode_tc_kernel" if decode_kernel == "tcgen05"
+                                    else "paged_decode_kernel") + " (store fused, split merge)",
                          "achieved": round(achieved, 1),
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4),
@@ -581,6 +585,33 @@ def run_profile(args):
 
     device = torch.device("cuda", 0)
     torch.cuda.set_device(device)
+    if args.profile == "long":
+        # BASELINE configs[4] run (b) shape on 4 layer pools (4 x 134 MB > L2)
+        layers, hq, hkv, ctx_len = 4, 32, 8, 32768
+        nb = ctx_len // BS
+        pool = mi.KVCache(layers, nb, BS, hkv, D, dtype=torch.bfloat16, device=device)
+        g = torch.Generator(device=device).manual_seed(5)
+        pool.keys.normal_(generator=g).mul_(0.5)
+        pool.values.normal_(generator=g).mul_(0.5)
+        table = torch.randperm(nb, generator=g, device=device).to(torch.int32).view(1, nb)
+        ctx = torch.tensor([ctx_len], dtype=torch.int32, device=device)
+        slots = (table[0, -1].long() * BS + BS - 1).to(torch.int32).view(1)
+        q = torch.randn(layers, 1, hq, D, generator=g, device=device).to(torch.bfloat16)
+        kn = torch.randn(layers, 1, hkv, D, generator=g, device=device).to(torch.bfloat16)
+        kernel, split, _ = mi.decode_plan(1, hq, hkv, D, torch.bfloat16, BS, args.split_k, device,
+                                          nb)
+        for _ in range(args.steps):
+            for i in range(layers):
+                view = pool.layer(i)
+                mi.paged_decode_store(q[i], view.keys, view.values, table, ctx, kn[i], kn[i],
+                                      slots, split_k=split)
+        torch.cuda.synchronize(device)
+        mi.check_device_status(device)
+        from oracle.paged_oracle import decode_bytes
+
+        print(json.dumps({"profile": "long", "kernel": kernel, "split_k": split,
+                          "decode_bytes_per_launch": decode_bytes([ctx_len], hq, hkv, D, 2, BS)}))
+        return
     if args.profile in ("prefill", "mixed"):
         workload = "prefix" if args.profile == "prefill" else "mixed"
         g = torch.Generator(device=device).manual_seed(11)
@@ -612,7 +643,8 @@ def run_profile(args):
     pool.values.normal_(generator=g).mul_(0.5)
     q = torch.randn(layers, NSEQ, HQ, D, generator=g, device=device).to(torch.bfloat16)
     kn = torch.randn(layers, NSEQ, HKV, D, generator=g, device=device).to(torch.bfloat16)
-    split = args.split_k or mi.select_split_k(NSEQ, HKV, device)
+    _, split, _ = mi.decode_plan(NSEQ, HQ, HKV, D, torch.bfloat16, BS, args.split_k, device,
+                                 table_d.shape[1])
     for _ in range(args.steps):
         for i in range(layers):
             view = pool.layer(i)
@@ -632,7 +664,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["decode", "prefill", "mixed"], default=None,
+    ap.add_argument("--profile", choices=["decode", "long", "prefill", "mixed"], default=None,
                     help="run a small eager case for ncu instead of the benchmark")
     ap.add_argument("--split-k", type=int, default=0)
     args = ap.parse_args()

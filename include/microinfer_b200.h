@@ -150,6 +150,22 @@ MI_API int mi_paged_decode(void *out, const void *query, const void *key_cache,
 MI_API int mi_paged_decode_uses_workspace(int32_t num_splits);
 
 /*
+ * Launch plan of mi_paged_decode / mi_paged_decode_store for a shape with
+ * 16-byte aligned tensors: returns the kernel (1 generic, 2 SIMT bulk-copy,
+ * 3 tcgen05 tensor-core) and writes the split count it will use for
+ * `num_splits` (0 = automatic) and the workspace bytes the caller must pass.
+ * The tensor-core kernel is chosen when the block table can address at least
+ * 2048 keys per sequence (block_table_stride * block_size); shorter contexts
+ * run the SIMT kernel.  MICROINFER_B200_DECODE=simt|tc pins one.
+ */
+MI_API int mi_paged_decode_plan(int64_t num_seqs, int32_t num_q_heads,
+                         int32_t num_kv_heads, int32_t head_dim,
+                         int32_t dtype, int32_t block_size,
+                         int64_t block_table_stride, int32_t num_splits,
+                         int device, int32_t *splits_out,
+                         size_t *workspace_bytes_out);
+
+/*
  * Paged decode with this step's store_kvcache fused in: for each sequence s
  * with slot_mapping[s] >= 0, k_new/v_new row s ([num_kv_heads, head_dim],
  * rows new_token_stride elements apart) is written to that slot of the pool,

@@ -19,6 +19,7 @@ from microinfer_b200._lib import check_device_status, load, read_device_status
 from microinfer_b200.install import install
 from microinfer_b200.layer.metadata import AttentionMetadata
 from microinfer_b200.layer.paged_attention import (
+    decode_plan,
     gather_paged_kv,
     paged_attention_meta,
     paged_decode,
@@ -36,6 +37,7 @@ __all__ = [
     "LayerKVCache",
     "check_device_status",
     "copy_blocks",
+    "decode_plan",
     "gather_paged_kv",
     "install",
     "load",

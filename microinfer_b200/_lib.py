@@ -50,6 +50,11 @@ SIGNATURES = {
          _SZ, _P, _P],
     ),
     "mi_paged_decode_uses_workspace": (ctypes.c_int, [_I32]),
+    "mi_paged_decode_plan": (
+        ctypes.c_int,
+        [_I64, _I32, _I32, _I32, _I32, _I32, _I64, _I32, ctypes.c_int, ctypes.POINTER(_I32),
+         ctypes.POINTER(_SZ)],
+    ),
     "mi_paged_decode_store": (
         ctypes.c_int,
         [_P, _P, _P, _P, _I64, _I32, _I32, _I32, _I32, _I32, _P, _I64, _P, _I64, _P, _P, _I64, _P,

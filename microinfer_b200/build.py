@@ -20,8 +20,8 @@ LIB_NAME = "libmicroinfer_b200.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 BUILD_DIR = PKG_DIR.parent / "_build"
 
-SOURCES = ["capi.cu", "copy_kernels.cu", "attention.cu", "decode.cu", "prefill_tc.cu",
-           "decode_noalloc.cu"]
+SOURCES = ["capi.cu", "copy_kernels.cu", "attention.cu", "decode.cu", "decode_tc.cu",
+           "prefill_tc.cu", "decode_noalloc.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [
     "-O3",

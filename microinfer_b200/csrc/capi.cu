@@ -21,6 +21,9 @@ cudaError_t launch_wait_flag(const int32_t *flag, int64_t timeout_ns, int32_t *s
                              cudaStream_t stream);
 cudaError_t launch_attn_generic(const AttnParams &p, int dtype, bool paged, cudaStream_t stream);
 bool decode_fast_supported(int dtype, int D, int G);
+bool decode_tc_supported(int dtype, int D, int G, int block_size);
+cudaError_t launch_decode_tc(const DecodeParams &d, int dtype, int G, int64_t num_seqs,
+                             int64_t num_blocks, int nsplit, cudaStream_t stream);
 cudaError_t launch_decode_fast(const DecodeParams &p, int dtype, int D, int G, int64_t num_seqs,
                                int nsplit, cudaStream_t stream);
 bool prefill_tc_supported(int dtype, int D, int G, int block_size);
@@ -204,8 +207,14 @@ int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads, int32
   const int64_t sms = sm_count_of(device < 0 ? 0 : device);
   const int64_t base = num_seqs * num_kv_heads;
   // Two decode CTAs fit per SM; stay within that single wave (a second,
-  // partial wave doubles the latency of a short decode).
-  int64_t s = (2 * sms) / base;
+  // partial wave doubles the latency of a short decode).  With
+  // MICROINFER_B200_DECODE_CTAS_PER_SM=1 a layer fills only half the slots,
+  // leaving the other half to the next layer's early page loads.
+  static const int64_t per_sm = [] {
+    const char *v = std::getenv("MICROINFER_B200_DECODE_CTAS_PER_SM");
+    return (v != nullptr && std::strcmp(v, "1") == 0) ? 1 : 2;
+  }();
+  int64_t s = (per_sm * sms) / base;
   if (max_context_hint > 0) {
     const int64_t chunks = (static_cast<int64_t>(max_context_hint) + 15) / 16;
     const int64_t cap = chunks / 8;  // keep >= 2 chunks per warp (4 warps)
@@ -231,6 +240,43 @@ bool cluster_enabled() {
 // 2..8 splits merge through a thread-block cluster (no workspace); more
 // splits (or clusters switched off) use the workspace + combine kernel.
 bool decode_uses_workspace(int nsplit) { return nsplit > 1 && !(cluster_enabled() && nsplit <= 8); }
+
+// Decode kernels, in order of preference: tcgen05 (tensor-core, D=128 fp16 /
+// bf16, block size a multiple of 16), SIMT (bulk-copy staged, CUDA cores),
+// generic (any shape).  MICROINFER_B200_DECODE=simt|tc pins one.
+constexpr int kDecodeGeneric = 1, kDecodeSimt = 2, kDecodeTc = 3;
+
+// Contexts of at least this many keys (bounded by the block-table width)
+// stream long enough for the tensor-core kernel to win; shorter ones are
+// latency-bound and run on the SIMT kernel, which is quicker to start.
+constexpr int64_t kTcMinContext = 2048;
+
+int decode_kernel_for(int dtype, int D, int G, int block_size, bool aligned, int64_t max_context) {
+  static const int mode = [] {
+    const char *v = std::getenv("MICROINFER_B200_DECODE");
+    if (v != nullptr && std::strcmp(v, "simt") == 0) return 1;
+    if (v != nullptr && std::strcmp(v, "tc") == 0) return 2;
+    return 0;
+  }();
+  if (!aligned || !decode_fast_supported(dtype, D, G)) return kDecodeGeneric;
+  const bool tc_ok = decode_tc_supported(dtype, D, G, block_size);
+  if (mode == 2 && tc_ok) return kDecodeTc;
+  if (mode == 0 && tc_ok && max_context >= kTcMinContext) return kDecodeTc;
+  return kDecodeSimt;
+}
+
+// Split count: the caller's, else enough CTAs for one wave (the tcgen05
+// kernel holds one CTA per SM, the SIMT kernel two).
+int decode_splits_for(int kernel, int64_t num_seqs, int num_kv_heads, int num_splits, int dev) {
+  if (num_splits > 0) return num_splits;
+  if (kernel == kDecodeGeneric) return 1;
+  if (kernel == kDecodeSimt) return mi_paged_decode_default_splits(num_seqs, num_kv_heads, 0, dev);
+  const int64_t base = num_seqs * num_kv_heads;
+  int64_t s = sm_count_of(dev) / base;
+  if (s < 1) s = 1;
+  if (s > 64) s = 64;
+  return static_cast<int>(s);
+}
 
 struct NewToken {
   const void *k_new;
@@ -261,16 +307,21 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
     return fail(MI_ERR_INVALID, "null pointer");
   if (nt != nullptr && (!nt->k_new || !nt->v_new || !nt->slots || nt->stride < 0))
     return fail(MI_ERR_INVALID, "fused store needs k_new, v_new, slot_mapping and a stride >= 0");
-  if (decode_uses_workspace(num_splits) &&
+  const int G = num_q_heads / num_kv_heads;
+  const bool aligned = aligned16(key_cache) && aligned16(value_cache) && aligned16(query);
+  // A sequence's context cannot exceed its block-table row.
+  const int kernel =
+      decode_kernel_for(dtype, head_dim, G, block_size, aligned, block_table_stride * block_size);
+  const bool fast = kernel != kDecodeGeneric;
+  if (fast && num_splits > 0 && decode_uses_workspace(num_splits) &&
       (workspace == nullptr ||
        workspace_bytes < mi_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, num_splits)))
     return fail(MI_ERR_INVALID, "workspace too small for num_splits (see "
                                 "mi_paged_decode_workspace_bytes)");
   if (const int s = select_device(key_cache)) return s;
-  const int G = num_q_heads / num_kv_heads;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const bool fast = decode_fast_supported(dtype, head_dim, G) && aligned16(key_cache) &&
-                    aligned16(value_cache) && aligned16(query);
+  int dev = 0;
+  cudaGetDevice(&dev);
   // The fused store reads k_new/v_new rows with 16-byte loads.
   const bool fuse_store = nt != nullptr && fast && aligned16(nt->k_new) && aligned16(nt->v_new) &&
                           (nt->stride * e) % 16 == 0;
@@ -314,10 +365,7 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
     p.status = dev_status;
     return cuda_status(launch_attn_generic(p, dtype, true, st));
   }
-  int dev = 0;
-  cudaGetDevice(&dev);
-  int nsplit = num_splits == 0 ? mi_paged_decode_default_splits(num_seqs, num_kv_heads, 0, dev)
-                               : num_splits;
+  const int nsplit = decode_splits_for(kernel, num_seqs, num_kv_heads, num_splits, dev);
   DecodeParams p = {};
   p.out = out;
   p.query = query;
@@ -354,6 +402,10 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
   if (flags & MI_DECODE_EARLY_KV) {
     p.early_kv = 1;
   }
+  if (kernel == kDecodeTc) {
+    const cudaError_t te = launch_decode_tc(p, dtype, G, num_seqs, num_blocks, nsplit, st);
+    if (te != cudaErrorNotSupported) return cuda_status(te);
+  }
   return cuda_status(launch_decode_fast(p, dtype, head_dim, G, num_seqs, nsplit, st));
 }
 
@@ -363,6 +415,25 @@ extern "C" {
 
 int mi_paged_decode_uses_workspace(int32_t num_splits) {
   return decode_uses_workspace(num_splits) ? 1 : 0;
+}
+
+int mi_paged_decode_plan(int64_t num_seqs, int32_t num_q_heads, int32_t num_kv_heads,
+                         int32_t head_dim, int32_t dtype, int32_t block_size,
+                         int64_t block_table_stride, int32_t num_splits, int device,
+                         int32_t *splits_out, size_t *workspace_bytes_out) {
+  if (elem_size(dtype) == 0 || num_seqs < 0 || num_q_heads <= 0 || num_kv_heads <= 0 ||
+      head_dim <= 0 || head_dim > 256 || num_q_heads % num_kv_heads != 0 || block_size <= 0 ||
+      block_table_stride < 0 || num_splits < 0 || num_splits > 1024)
+    return fail(MI_ERR_INVALID, "invalid decode shape");
+  const int kernel = decode_kernel_for(dtype, head_dim, num_q_heads / num_kv_heads, block_size, true,
+                                       block_table_stride * block_size);
+  const int s = decode_splits_for(kernel, num_seqs, num_kv_heads, num_splits, device < 0 ? 0 : device);
+  if (splits_out) *splits_out = s;
+  if (workspace_bytes_out)
+    *workspace_bytes_out = (kernel != kDecodeGeneric && decode_uses_workspace(s))
+                               ? mi_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, s)
+                               : 0;
+  return kernel;
 }
 
 int mi_paged_decode(void *out, const void *query, const void *key_cache, const void *value_cache,

@@ -612,6 +612,16 @@ static cudaError_t launch_decode_td(const DecodeParams &p, int G, int64_t n, int
   return cudaErrorInvalidValue;
 }
 
+cudaError_t launch_decode_combine(const DecodeParams &p, int dtype, int D, int64_t num_seqs,
+                                  int nsplit, cudaStream_t stream) {
+  const dim3 grid(p.num_q_heads, static_cast<unsigned>(num_seqs));
+  if (dtype == MI_DTYPE_FLOAT32)
+    return launch_pdl(decode_combine_kernel<float>, grid, dim3(128), 0, stream, p, nsplit, D);
+  if (dtype == MI_DTYPE_FLOAT16)
+    return launch_pdl(decode_combine_kernel<__half>, grid, dim3(128), 0, stream, p, nsplit, D);
+  return launch_pdl(decode_combine_kernel<__nv_bfloat16>, grid, dim3(128), 0, stream, p, nsplit, D);
+}
+
 bool decode_fast_supported(int dtype, int D, int G) {
   if (G != 1 && G != 2 && G != 4 && G != 8) return false;
   if (dtype == MI_DTYPE_FLOAT32) return D == 64 || D == 128;

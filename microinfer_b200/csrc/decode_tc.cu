@@ -1,0 +1,663 @@
+// tcgen05 paged decode attention (sm_100a), "swap-AB" form.
+//
+// Decode has 1..8 query rows per kv head, far below the 128-row MMA tile, so
+// the roles of keys and queries are swapped: per 128-key tile
+//     S^T[128 keys x 16] = K_tile[128 x D] . Q^T[D x 16]     (M=128, N=16, K=D)
+//     O^T[D x 16]       += V_tile^T[D x 128] . P^T[128 x 16] (M=D,  N=16, K=128)
+// with the GQA group in the N dimension (padded to 16; the padding columns
+// are never read).  The tensor core does all the multiply-adds, so the SMs
+// only run a short softmax per tile and the kernel stays HBM-bound.
+//
+// One CTA per (split, kv head, sequence); split s owns key tiles s, s+S, ...
+// 224 threads:
+//   warp 0    K producer: TMA of 8 groups of 16 keys per tile (3-D map over
+//             [slots, Hkv, D], slot from the block table, zero fill past the
+//             context) into a 3-stage ring; the G query rows; the fused store
+//             of this step's token.
+//   warp 6    V producer: the same for V, so K runs ahead of V (K frees after
+//             the S MMA, V only after P.V).
+//   warp 1    TMEM owner (64 columns) and single-thread MMA issuer, issuing
+//             whichever of S(next) and P.V(next) is ready first.
+//   warps 2-5 softmax, one key per thread: scores from TMEM, per-head tile
+//             max (warp shuffle + a 128-thread barrier exchange), lazy rescale
+//             of O^T (only when a head's max grows by more than 2^8), P^T
+//             (double-buffered) written as the B operand of the next MMA;
+//             epilogue with one head dimension per thread.
+// Splits merge through a thread-block cluster (2..8) or a workspace.  Every
+// wait is bounded; the softmax warps abort together (barrier.red.or), so no
+// warp is ever left at a barrier.
+#include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "launch.cuh"
+#include "params.cuh"
+#include "tc_helpers.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace mi {
+
+struct __align__(64) DecodeTcParams {
+  CUtensorMap tmap_q;
+  CUtensorMap tmap_k;
+  CUtensorMap tmap_v;
+  DecodeParams d;
+  int64_t kv_rows;  // extent of the K/V maps' row dimension (OOB coordinate)
+};
+
+namespace {
+
+constexpr int kThreads = 224;
+constexpr int kStages = 3;
+constexpr int kTile = 32768;  // 128 keys x 128 dims x 2 bytes
+constexpr int kHalf = 16384;
+constexpr int kPBytes = 4096;  // P^T: 16 rows x 128 keys x 2 bytes
+constexpr int kOffQ = 0;       // 16 rows x 128 dims: two 2 KB column halves
+constexpr int kOffK = 4096;
+constexpr int kOffV = kOffK + kStages * kTile;
+constexpr int kOffP = kOffV + kStages * kTile;  // 2 buffers
+constexpr int kOffRed = kOffP + 2 * kPBytes;    // [2][4 warps][8 heads] + [4][8]
+constexpr int kOffBar = kOffRed + 1024;
+constexpr int kSmemBytes = kOffBar + 256 + 1024;
+constexpr uint32_t kTmemCols = 64;  // S^T x2 (16 each) + O^T (16)
+constexpr unsigned kFull = 0xffffffffu;
+
+enum {
+  B_Q = 0,
+  B_KFULL = 1,    // +stage (3)
+  B_VFULL = 4,    // +stage
+  B_KEMPTY = 7,   // +stage
+  B_VEMPTY = 10,  // +stage
+  B_SFULL = 13,   // +S buffer (2)
+  B_SEMPTY = 15,  // +S buffer
+  B_PFULL = 17,   // +P buffer (2)
+  B_ODONE = 19,   // +P buffer: P.V of tiles with that parity done
+  B_FIN = 21,
+  B_STORED = 22,  // the fused store of this step's token is visible
+  B_COUNT = 23
+};
+
+__device__ __forceinline__ uint64_t k_desc(uint32_t tile, int kk) {  // K tile, K-major
+  return tc::smem_desc_sw128(tile + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
+}
+__device__ __forceinline__ uint64_t small_desc(uint32_t base, int kk) {  // 16-row K-major (Q, P^T)
+  return tc::smem_desc_sw128(base + (kk >> 2) * 2048 + (kk & 3) * 32, 16, 1024);
+}
+__device__ __forceinline__ uint64_t v_desc(uint32_t tile, int kk) {  // V^T as MN-major A
+  return tc::smem_desc_sw128(tile + kk * 2048, kHalf, 1024);
+}
+
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(kFull, x, o));
+  return x;
+}
+__device__ __forceinline__ float warp_sum(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(kFull, x, o);
+  return x;
+}
+
+// Barrier over the 4 softmax warps (id 1, 128 threads) that also ORs `bad`.
+__device__ __forceinline__ bool softmax_sync_any(bool bad) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pin, pout;\n\tsetp.ne.u32 pin, %1, 0;\n\t"
+      "bar.red.or.pred pout, 1, 128, pin;\n\tselp.u32 %0, 1, 0, pout;\n\t}"
+      : "=r"(r)
+      : "r"(bad ? 1u : 0u)
+      : "memory");
+  return r != 0;
+}
+
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+}  // namespace
+
+template <typename T, int G>
+__global__ void __launch_bounds__(kThreads, 1)
+    paged_decode_tc_kernel(const __grid_constant__ DecodeTcParams P) {
+  const DecodeParams &p = P.d;
+  constexpr bool kBf16 = Elem<T>::kDtype == MI_DTYPE_BFLOAT16;
+  constexpr uint32_t kIdescS = tc::idesc_f16(128, 16, kBf16 ? 1 : 0, false, false);
+  constexpr uint32_t kIdescO = tc::idesc_f16(128, 16, kBf16 ? 1 : 0, false, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kOffBar);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + B_COUNT);
+  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+  float *red = reinterpret_cast<float *>(smem + kOffRed);  // [2][4][8] then [4][8]
+  const uint32_t sQ = smem_addr(smem + kOffQ);
+  const uint32_t sK = smem_addr(smem + kOffK);
+  const uint32_t sV = smem_addr(smem + kOffV);
+  const uint32_t sP = smem_addr(smem + kOffP);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, nsplit = gridDim.x;
+  const int kvh = blockIdx.y;
+  const int64_t seq = blockIdx.z;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[B_Q], 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&bar[B_KFULL + s], 1);
+      mbar_init(&bar[B_VFULL + s], 1);
+      mbar_init(&bar[B_KEMPTY + s], 1);
+      mbar_init(&bar[B_VEMPTY + s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar[B_SFULL + b], 1);
+      mbar_init(&bar[B_SEMPTY + b], 128);
+      mbar_init(&bar[B_PFULL + b], 128);
+      mbar_init(&bar[B_ODONE + b], 1);
+    }
+    mbar_init(&bar[B_FIN], 1);
+    mbar_init(&bar[B_STORED], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) tc::tmem_alloc(tmem_slot, kTmemCols);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem, tO = tmem + 32;
+
+  // Without early_kv everything below may come from the preceding kernel.
+  if (!p.early_kv) pdl_wait();
+  int ctx = p.context_lens[seq];
+  const int64_t cap = p.bt_stride * p.block_size;
+  if (ctx > cap) {
+    if (threadIdx.x == 0 && split == 0) flag_status(p.status, MI_DEV_BAD_BLOCK);
+    ctx = static_cast<int>(cap);
+  }
+  const int ntiles = ctx > 0 ? (ctx + 127) / 128 : 0;
+  const int my_n = split < ntiles ? (ntiles - split + nsplit - 1) / nsplit : 0;
+  const int last_tile = ntiles - 1;
+  const int64_t slot = p.k_new != nullptr ? static_cast<int64_t>(p.slot_mapping[seq]) : -1;
+  const bool own_last = slot >= 0 && last_tile >= 0 && last_tile % nsplit == split;
+  auto tile_of = [&](int it) { return split + nsplit * it; };
+
+  if (warp == 0 || warp == 6) {
+    // ------------------------------------------------------------ producers
+    const bool is_v = warp == 6;
+    const int32_t *table = p.block_tables + seq * p.bt_stride;
+    const CUtensorMap *map = is_v ? &P.tmap_v : &P.tmap_k;
+    uint8_t *ring = smem + (is_v ? kOffV : kOffK);
+    uint64_t *full_b = &bar[is_v ? B_VFULL : B_KFULL];
+    uint64_t *empty_b = &bar[is_v ? B_VEMPTY : B_KEMPTY];
+    const int g = lane >> 1, dh = lane & 1;  // lanes 0..15: (16-key group, column half)
+    auto row_of = [&](int it) -> int {
+      if (lane >= 16 || it >= my_n) return 0;
+      const int key0 = tile_of(it) * 128 + g * 16;
+      if (key0 >= ctx) return static_cast<int>(P.kv_rows);  // zero fill
+      const int64_t col = key0 / p.block_size;
+      const int64_t blk = col < p.bt_stride ? table[col] : -1;
+      if (blk < 0 || blk >= p.num_blocks) {
+        flag_status(p.status, MI_DEV_BAD_BLOCK);
+        return static_cast<int>(P.kv_rows);
+      }
+      return static_cast<int>(blk * p.block_size + key0 % p.block_size);
+    };
+    auto load = [&](int it, int row) -> bool {
+      const int s = it % kStages;
+      int good = 1;
+      if (lane == 0)
+        good = mbar_wait_bounded(&empty_b[s], ((it / kStages) & 1) ^ 1, p.status) &&
+               !*(volatile int *)abort_flag;
+      if (!__shfl_sync(kFull, good, 0)) return false;
+      if (lane == 0) mbar_arrive_expect_tx(&full_b[s], kTile);
+      __syncwarp();
+      if (lane < 16)
+        tc::tma_load_3d(ring + s * kTile + dh * kHalf + g * 2048, map, dh * 64, kvh, row, &full_b[s]);
+      return true;
+    };
+    // This step's token (head kvh) goes to the pool before its tile is copied.
+    auto store_token = [&]() {
+      if (slot < p.num_blocks * p.block_size) {
+        const int kind = lane >> 4, chunk = lane & 15;  // 2 x 16 pieces of 16 bytes
+        const char *src = (kind ? p.v_new : p.k_new) + seq * p.new_token_stride_bytes +
+                          static_cast<int64_t>(kvh) * 256 + chunk * 16;
+        char *dst = const_cast<char *>(kind ? p.value_cache : p.key_cache) +
+                    (slot * p.num_kv_heads + kvh) * 256 + chunk * 16;
+        *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+      } else if (lane == 0) {
+        flag_status(p.status, MI_DEV_BAD_SLOT);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar[B_STORED]);
+    };
+    // Before loading the new token's tile: K producer stores it, V producer
+    // waits until the store is visible.
+    auto before_new_tile = [&]() -> bool {
+      if (!is_v) {
+        store_token();
+        return true;
+      }
+      int good = 1;
+      if (lane == 0) good = mbar_wait_bounded(&bar[B_STORED], 0, p.status);
+      return __shfl_sync(kFull, good, 0) != 0;
+    };
+    if (lane == 0) tc::prefetch_tmap(map);
+    bool ok = true;
+    int deferred = -1;
+    int row = row_of(0);
+    int it = 0;
+    for (; it < kStages && it < my_n && ok; ++it) {
+      const int next_row = row_of(it + 1);
+      const bool new_tile = own_last && tile_of(it) == last_tile;
+      if (new_tile && p.early_kv) {
+        deferred = it;
+      } else {
+        if (new_tile) ok = before_new_tile();
+        if (ok) ok = load(it, row);
+      }
+      row = next_row;
+    }
+    if (p.early_kv) {
+      if (!is_v) pdl_launch_dependents();
+      pdl_wait();
+      if (deferred >= 0 && ok) {
+        ok = before_new_tile();
+        if (ok) ok = load(deferred, row_of(deferred));
+      }
+    }
+    if (!is_v && lane == 0) {
+      mbar_arrive_expect_tx(&bar[B_Q], 2 * G * 128);
+      for (int h2 = 0; h2 < 2; ++h2)
+        tc::tma_load_3d(smem + kOffQ + h2 * 2048, &P.tmap_q, h2 * 64, kvh * G,
+                        static_cast<int>(seq), &bar[B_Q]);
+    }
+    for (; it < my_n && ok; ++it) {
+      const int next_row = row_of(it + 1);  // table lookup of the next tile overlaps the wait
+      if (own_last && tile_of(it) == last_tile) ok = before_new_tile();
+      if (ok) ok = load(it, row);
+      row = next_row;
+    }
+    if (!ok && lane == 0) *(volatile int *)abort_flag = 1;
+    // Every load this warp issued lands before the CTA can exit.
+    if (lane == 0) {
+      const int issued = ok ? my_n : it;
+      for (int j = max(0, issued - kStages); j < issued; ++j)
+        mbar_wait_bounded(&full_b[j % kStages], (j / kStages) & 1, p.status);
+      if (!is_v) mbar_wait_bounded(&bar[B_Q], 0, p.status);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait_bounded(&bar[B_Q], 0, p.status);
+      int ns = 0, npv = 0;  // next S tile, next P.V tile
+      uint64_t since = global_ns();
+      while (ok && npv < my_n) {
+        bool progress = false;
+        if (ns < my_n) {
+          const int s = ns % kStages, b = ns & 1;
+          if (mbar_test(&bar[B_KFULL + s], (ns / kStages) & 1) &&
+              mbar_test(&bar[B_SEMPTY + b], ((ns >> 1) & 1) ^ 1)) {
+            tc::fence_after_sync();
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              tc::umma_f16(tS + b * 16, k_desc(sK + s * kTile, kk), small_desc(sQ, kk), kIdescS,
+                           kk > 0 ? 1u : 0u);
+            tc::umma_commit(&bar[B_SFULL + b]);
+            tc::umma_commit(&bar[B_KEMPTY + s]);
+            ++ns;
+            progress = true;
+          }
+        }
+        if (npv < ns) {
+          const int s = npv % kStages, pb = npv & 1;
+          if (mbar_test(&bar[B_PFULL + pb], (npv >> 1) & 1) &&
+              mbar_test(&bar[B_VFULL + s], (npv / kStages) & 1)) {
+            tc::fence_after_sync();
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              tc::umma_f16(tO, v_desc(sV + s * kTile, kk), small_desc(sP + pb * kPBytes, kk),
+                           kIdescO, (npv > 0 || kk > 0) ? 1u : 0u);
+            tc::umma_commit(&bar[B_ODONE + pb]);
+            tc::umma_commit(&bar[B_VEMPTY + s]);
+            ++npv;
+            progress = true;
+          }
+        }
+        if (progress) {
+          since = global_ns();
+        } else {
+          if (*(volatile int *)abort_flag) {
+            ok = false;
+          } else if (global_ns() - since > kWaitLimitNs) {
+            flag_status(p.status, MI_DEV_TIMEOUT);
+            ok = false;
+          } else {
+            __nanosleep(32);
+          }
+        }
+      }
+      if (!ok) *(volatile int *)abort_flag = 1;
+      tc::umma_commit(&bar[B_FIN]);
+      mbar_wait_bounded(&bar[B_FIN], 0, p.status);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int q4 = warp & 3;
+    const int k = q4 * 32 + lane;  // key of the tile (S^T lane) / dimension (O^T lane)
+    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    float m[G], lp[G];
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      m[h] = -INFINITY;
+      lp[h] = 0.f;
+    }
+    bool ok = true;
+    for (int it = 0; it < my_n; ++it) {
+      const int b = it & 1;
+      const bool good = __all_sync(kFull, mbar_wait_bounded(&bar[B_SFULL + b], (it >> 1) & 1, p.status) &&
+                                              !*(volatile int *)abort_flag);
+      float sv[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) sv[i] = 0.f;
+      if (good) {
+        tc::fence_after_sync();
+        tc::tmem_ld16(tS + b * 16 + lane_off, sv);
+        tc::tmem_wait_ld();
+        tc::fence_before_sync();
+      }
+      mbar_arrive(&bar[B_SEMPTY + b]);
+
+      const bool valid = tile_of(it) * 128 + k < ctx;
+      float x[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) x[h] = valid ? sv[h] * p.scale_log2 : -INFINITY;
+      // per-head max of this tile over all 128 keys
+      float *rb = red + b * 32;
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float wm = warp_max(x[h]);
+        if (lane == 0) rb[q4 * 8 + h] = wm;
+      }
+      if (softmax_sync_any(!good)) {  // also publishes rb to the other warps
+        ok = false;
+        break;
+      }
+      float mn[G], alpha[G];
+      bool rescale = false;
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float tm = fmaxf(fmaxf(rb[h], rb[8 + h]), fmaxf(rb[16 + h], rb[24 + h]));
+        mn[h] = tm > m[h] + 8.f ? tm : m[h];
+        alpha[h] = mn[h] == m[h] ? 1.f : (m[h] == -INFINITY ? 0.f : fast_exp2(m[h] - mn[h]));
+        rescale |= mn[h] != m[h] && m[h] != -INFINITY;
+      }
+      float pv[G];
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        pv[h] = x[h] == -INFINITY ? 0.f : fast_exp2(x[h] - mn[h]);
+        lp[h] = lp[h] * alpha[h] + pv[h];
+      }
+      // Rescaling O^T needs the previous tile's P.V done; reusing P^T buffer b
+      // needs the P.V two tiles back done.  Both decisions are CTA-uniform.
+      const bool need_r = rescale && it >= 1, need_p = it >= 2;
+      if (need_r || need_p) {
+        bool w = true;
+        if (need_r) w &= mbar_wait_bounded(&bar[B_ODONE + ((it - 1) & 1)], ((it - 1) >> 1) & 1, p.status);
+        if (need_p) w &= mbar_wait_bounded(&bar[B_ODONE + b], ((it - 2) >> 1) & 1, p.status);
+        if (softmax_sync_any(!__all_sync(kFull, w))) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        if (need_r) {
+          float o[16];
+          tc::tmem_ld16(tO + lane_off, o);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int h = 0; h < G; ++h) o[h] *= alpha[h];
+          tc::tmem_st16(tO + lane_off, o);
+          tc::tmem_wait_st();
+        }
+      }
+      const uint32_t pbase = sP + b * kPBytes;
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const uint32_t addr = pbase + (k >> 6) * 2048 + h * 128 +
+                              ((((k & 63) >> 3) ^ (h & 7)) << 4) + (k & 7) * 2;
+        const T v = Elem<T>::from_float(pv[h]);
+        asm volatile("st.shared.b16 [%0], %1;" ::"r"(addr),
+                     "h"(*reinterpret_cast<const unsigned short *>(&v))
+                     : "memory");
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc::fence_before_sync();
+      mbar_arrive(&bar[B_PFULL + b]);
+#pragma unroll
+      for (int h = 0; h < G; ++h) m[h] = mn[h];
+    }
+    // ---- epilogue: thread k holds head dimension d = k of O^T ----
+    float o[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i] = 0.f;
+    if (ok && my_n > 0) {
+      const int last = my_n - 1;
+      const bool w = __all_sync(kFull, mbar_wait_bounded(&bar[B_ODONE + (last & 1)], (last >> 1) & 1, p.status));
+      ok = !softmax_sync_any(!w);
+      if (ok) {
+        tc::fence_after_sync();
+        tc::tmem_ld16(tO + lane_off, o);
+        tc::tmem_wait_ld();
+      }
+    }
+    if (!ok) {
+      if (lane == 0) *(volatile int *)abort_flag = 1;
+#pragma unroll
+      for (int h = 0; h < G; ++h) m[h] = -INFINITY;
+    }
+    float *lred = red + 64;
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float s = warp_sum(lp[h]);
+      if (lane == 0) lred[q4 * 8 + h] = s;
+    }
+    softmax_sync_any(false);
+    const int d = k;
+    float *fin_acc = reinterpret_cast<float *>(smem + kOffK);  // aliases the drained K ring
+    float *fin_ml = fin_acc + 8 * 128;
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      const float L = lred[h] + lred[8 + h] + lred[16 + h] + lred[24 + h];
+      const float M = m[h];
+      const int qh = kvh * G + h;
+      if (nsplit == 1) {
+        T *orow = static_cast<T *>(p.out) + (seq * p.num_q_heads + qh) * 128;
+        orow[d] = Elem<T>::from_float(L > 0.f ? o[h] / L : 0.f);
+      } else if (p.cluster_combine) {
+        fin_acc[h * 128 + d] = o[h];
+        if (d == 0) {
+          fin_ml[h * 2] = M;
+          fin_ml[h * 2 + 1] = L;
+        }
+      } else {
+        const int64_t state = (seq * p.num_q_heads + qh) * nsplit + split;
+        p.ws_acc[state * 128 + d] = o[h];
+        if (d == 0) {
+          p.ws_ml[state * 2] = M;
+          p.ws_ml[state * 2 + 1] = L;
+        }
+      }
+    }
+  }
+
+  pdl_launch_dependents();
+  tc::fence_before_sync();
+  __syncthreads();
+  if (p.cluster_combine && nsplit > 1) {
+    cg::cluster_group cluster = cg::this_cluster();
+    float *fin_acc = reinterpret_cast<float *>(smem + kOffK);
+    float *fin_ml = fin_acc + 8 * 128;
+    cluster.sync();
+    for (int i = split * kThreads + threadIdx.x; i < G * 128; i += nsplit * kThreads) {
+      const int h = i / 128, d = i % 128;
+      float ms[8], ls[8], as[8];
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        if (s < nsplit) {
+          const float *rml = cluster.map_shared_rank(fin_ml, s);
+          ms[s] = rml[h * 2];
+          ls[s] = rml[h * 2 + 1];
+          as[s] = cluster.map_shared_rank(fin_acc, s)[h * 128 + d];
+        }
+      }
+      float M = -INFINITY;
+#pragma unroll
+      for (int s = 0; s < 8; ++s)
+        if (s < nsplit) M = fmaxf(M, ms[s]);
+      float L = 0.f, A = 0.f;
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        if (s < nsplit) {
+          const float f = ms[s] == -INFINITY ? 0.f : fast_exp2(ms[s] - M);
+          L += f * ls[s];
+          A += f * as[s];
+        }
+      }
+      T *orow = static_cast<T *>(p.out) + (seq * p.num_q_heads + kvh * G + h) * 128;
+      orow[d] = Elem<T>::from_float(L > 0.f ? A / L : 0.f);
+    }
+    cluster.sync();
+  }
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn_dec() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+bool encode(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t heads,
+            uint64_t rows, uint64_t row_stride_bytes, uint32_t box_y, uint32_t box_z) {
+  auto fn = encode_fn_dec();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {128, heads, rows};
+  cuuint64_t strides[2] = {256, row_stride_bytes};
+  cuuint32_t box[3] = {64, box_y, box_z};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, dt, 3, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename T, int G>
+cudaError_t launch_tg(const DecodeTcParams &P, int64_t num_seqs, int nsplit, cudaStream_t stream) {
+  auto kern = paged_decode_tc_kernel<T, G>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nsplit, P.d.num_kv_heads, static_cast<unsigned>(num_seqs));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (P.d.cluster_combine && nsplit > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = nsplit;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, P);
+}
+
+}  // namespace
+
+cudaError_t launch_decode_combine(const DecodeParams &p, int dtype, int D, int64_t num_seqs,
+                                  int nsplit, cudaStream_t stream);
+
+bool decode_tc_supported(int dtype, int D, int G, int block_size) {
+  if (dtype != MI_DTYPE_BFLOAT16 && dtype != MI_DTYPE_FLOAT16) return false;
+  if (D != 128 || (G != 1 && G != 2 && G != 4 && G != 8)) return false;
+  if (block_size < 16 || block_size % 16 != 0) return false;
+  return encode_fn_dec() != nullptr;
+}
+
+cudaError_t launch_decode_tc(const DecodeParams &d, int dtype, int G, int64_t num_seqs,
+                             int64_t num_blocks, int nsplit, cudaStream_t stream) {
+  if (num_seqs > 65535 || nsplit > 65535) return cudaErrorNotSupported;
+  const CUtensorMapDataType dt =
+      dtype == MI_DTYPE_BFLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  DecodeTcParams P;
+  memset(&P, 0, sizeof(P));
+  const uint64_t rows = static_cast<uint64_t>(num_blocks) * d.block_size;
+  if (rows == 0 || rows >= (1ull << 31)) return cudaErrorNotSupported;
+  if (!encode(&P.tmap_q, dt, d.query, d.num_q_heads, num_seqs,
+              static_cast<uint64_t>(d.num_q_heads) * 256, G, 1) ||
+      !encode(&P.tmap_k, dt, d.key_cache, d.num_kv_heads, rows,
+              static_cast<uint64_t>(d.num_kv_heads) * 256, 1, 16) ||
+      !encode(&P.tmap_v, dt, d.value_cache, d.num_kv_heads, rows,
+              static_cast<uint64_t>(d.num_kv_heads) * 256, 1, 16))
+    return cudaErrorInvalidValue;
+  P.d = d;
+  P.kv_rows = static_cast<int64_t>(rows);
+  cudaError_t e;
+  if (dtype == MI_DTYPE_BFLOAT16) {
+    switch (G) {
+      case 1: e = launch_tg<__nv_bfloat16, 1>(P, num_seqs, nsplit, stream); break;
+      case 2: e = launch_tg<__nv_bfloat16, 2>(P, num_seqs, nsplit, stream); break;
+      case 4: e = launch_tg<__nv_bfloat16, 4>(P, num_seqs, nsplit, stream); break;
+      default: e = launch_tg<__nv_bfloat16, 8>(P, num_seqs, nsplit, stream); break;
+    }
+  } else {
+    switch (G) {
+      case 1: e = launch_tg<__half, 1>(P, num_seqs, nsplit, stream); break;
+      case 2: e = launch_tg<__half, 2>(P, num_seqs, nsplit, stream); break;
+      case 4: e = launch_tg<__half, 4>(P, num_seqs, nsplit, stream); break;
+      default: e = launch_tg<__half, 8>(P, num_seqs, nsplit, stream); break;
+    }
+  }
+  if (e != cudaSuccess || nsplit == 1 || d.cluster_combine) return e;
+  return launch_decode_combine(d, dtype, 128, num_seqs, nsplit, stream);
+}
+
+}  // namespace mi

@@ -16,6 +16,7 @@ caching allocator (the graph pool during capture), like the reference.
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -66,6 +67,29 @@ def select_split_k(num_requests: int, num_kv_heads: int, device=None,
     return _lib.load().mi_paged_decode_default_splits(num_requests, num_kv_heads, max_context, dev)
 
 
+DECODE_KERNELS = {1: "generic", 2: "simt", 3: "tcgen05"}
+
+
+def decode_plan(num_requests: int, num_q_heads: int, num_kv_heads: int, head_dim: int,
+                dtype: torch.dtype, block_size: int, split_k: int = 0, device=None,
+                table_width: int = 0):
+    """(kernel name, split count, workspace bytes) the decode launch will use.
+
+    ``split_k=0`` lets the library size the split for one wave of CTAs;
+    ``table_width`` (block-table columns) bounds the context, which picks
+    between the tensor-core and SIMT kernels.
+    """
+    dev = 0 if device is None else (torch.device(device).index or 0)
+    splits = ctypes.c_int32(0)
+    ws = ctypes.c_size_t(0)
+    kernel = _lib.load().mi_paged_decode_plan(num_requests, num_q_heads, num_kv_heads, head_dim,
+                                              _lib.dtype_code(dtype), block_size, table_width,
+                                              split_k, dev, ctypes.byref(splits), ctypes.byref(ws))
+    if kernel < 0:
+        _lib.check(kernel)
+    return DECODE_KERNELS[kernel], splits.value, ws.value
+
+
 def _decode_prep(query, key_cache, value_cache, block_tables, context_lens, split_k, scale, out):
     num_q_heads, head_dim, block_size, num_kv_heads = _check_common(query, key_cache, value_cache)
     num_requests = query.shape[0]
@@ -75,16 +99,16 @@ def _decode_prep(query, key_cache, value_cache, block_tables, context_lens, spli
     if context_lens.numel() != num_requests:
         raise ValueError("context_lens must have one entry per request")
     if split_k is None:
-        split_k = select_split_k(num_requests, num_kv_heads, device)
-    if type(split_k) is not int or split_k <= 0:
-        raise ValueError("split_k must be a positive int")
+        split_k = 0
+    if type(split_k) is not int or split_k < 0:
+        raise ValueError("split_k must be a positive int (or None for automatic)")
     if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
         raise ValueError("KV caches must be contiguous")
-    lib = _lib.load()
-    ws_bytes = 0
+    _, split_k, ws_bytes = decode_plan(num_requests, num_q_heads, num_kv_heads, head_dim,
+                                       query.dtype, block_size, split_k, device,
+                                       block_tables.shape[1])
     workspace = None
-    if lib.mi_paged_decode_uses_workspace(split_k):
-        ws_bytes = lib.mi_paged_decode_workspace_bytes(num_requests, num_q_heads, head_dim, split_k)
+    if ws_bytes:
         workspace = torch.empty(ws_bytes // 4, dtype=torch.float32, device=device)
     return dict(
         query=query.contiguous(), block_tables=_idx(block_tables), context_lens=_idx(context_lens),

@@ -57,7 +57,9 @@ def test_workspace_and_split_policy():
 
 
 def _decode_args(**over):
-    args = dict(out=1, query=1, key_cache=1, value_cache=1, num_blocks=4, block_size=16,
+    # 16-byte aligned fake addresses: the shape goes to a fast kernel, and every
+    # rejection below happens on the host before any pointer is touched.
+    args = dict(out=256, query=256, key_cache=256, value_cache=256, num_blocks=4, block_size=16,
                 num_q_heads=16, num_kv_heads=8, head_dim=128, dtype=2, block_tables=1,
                 block_table_stride=4, context_lens=1, num_seqs=2, scale=0.1, num_splits=1,
                 workspace=None, workspace_bytes=0, dev_status=None, stream=None)
