@@ -44,6 +44,17 @@ def _peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
+def _profiled_traffic(summary: str):
+    """DRAM bytes per launch (read + write) recorded in a profiles/ ncu summary."""
+    try:
+        for line in (ROOT / "profiles" / summary).read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
 def make_batch(seed: int, device):
     """Seeded synthetic step on the device (torch generators, no host data)."""
     import torch
@@ -552,7 +563,12 @@ def run_ours(args):
                          "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "peak_source": f"hbm_gbs of {peak_src}",
                          "avg_launch_us": round(decode_launch_ms * 1e3, 3),
-                         "algorithmic_bytes_per_launch": dec_b + st_b, "traffic": None,
+                         "algorithmic_bytes_per_launch": dec_b + st_b,
+                         "traffic": _profiled_traffic(
+                             "decode_tc_qwen3_8b_32k.md" if decode_kernel == "tcgen05"
+                             else "decode_simt_qwen3_0.6b_config2.md"),
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
+                                           "profiles/ summary of the same kernel and shapes",
                          "step_frac": round(value / world / peaks["hbm_gbs"], 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
