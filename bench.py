@@ -537,8 +537,8 @@ def run_ours(args):
     e2e_value = world * step_bytes / (e2e_ms * 1e-3) / 1e9
     mi.check_device_status(device)
 
-    uses_ws = bool(mi.load().mi_paged_decode_uses_workspace(split))
-    launches_per_step = LAYERS * (1 + (1 if uses_ws else 0))
+    # one launch per layer (store and split merge are inside the decode kernel)
+    launches_per_step = LAYERS
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,

@@ -105,15 +105,25 @@ MI_API int mi_store_kv_slots(void *key_cache, void *value_cache, int64_t num_blo
 
 /*
  * Split-K decode workspace size in bytes for `num_splits` splits (0 when
- * num_splits == 1: the single-split kernel writes `out` directly).
+ * num_splits == 1: the single-split kernel writes `out` directly):
+ * 64 KiB of arrival counters, then num_seqs * num_q_heads * num_splits
+ * states of (head_dim + 2) floats.  The splits of one (sequence, kv head)
+ * store their softmax states and the last to finish merges them, then sets
+ * its counter back to zero: zero-fill a workspace once, before its first
+ * use, and it stays valid for every later launch of any shape.  Launches
+ * that can run at the same time (two streams) need separate workspaces.
+ * Split-K takes at most 16384 (sequence, kv head) pairs per launch.
  */
 MI_API size_t mi_paged_decode_workspace_bytes(int64_t num_seqs, int32_t num_q_heads,
                                        int32_t head_dim, int32_t num_splits);
 
 /*
- * Split count the decode launcher uses when the caller passes num_splits=0:
- * enough (seq, kv-head, split) CTAs to fill every SM twice, capped so each
- * split keeps >= 2 key chunks when `max_context_hint` > 0 is known.
+ * Split count the decode launcher uses when the caller passes num_splits=0.
+ * When num_seqs * num_kv_heads fits in half the SMs, the layer's CTAs stay
+ * within that half (one CTA per SM), so the next layer's CTAs fit beside
+ * them and request their pages early; with `max_context_hint` > 0 each split
+ * keeps >= 384 keys.  Larger batches fill every SM with two CTAs, each split
+ * keeping >= 2 chunks of 8 keys per warp.
  */
 MI_API int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads,
                                    int32_t max_context_hint, int device);
@@ -125,9 +135,9 @@ MI_API int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads
  * with GQA kv head h / (num_q_heads / num_kv_heads).  Replaces
  * triton_paged_decode + _paged_decode_kernel + _paged_decode_reduce_kernel,
  * microinfer/layer/triton_paged_attention.py:352-457 (:39-131, :235-257).
- * num_splits > 8 uses `workspace` (mi_paged_decode_workspace_bytes) and a
- * combine kernel, 2..8 splits merge in a thread-block cluster (see
- * mi_paged_decode_uses_workspace); num_splits == 0 picks
+ * num_splits > 1 needs `workspace` (mi_paged_decode_workspace_bytes,
+ * zero-filled before its first use); the last split of each (sequence,
+ * kv head) merges the states in the same launch.  num_splits == 0 picks
  * mi_paged_decode_default_splits.
  * Query and out are contiguous [num_seqs, num_q_heads, head_dim].
  */
@@ -141,11 +151,8 @@ MI_API int mi_paged_decode(void *out, const void *query, const void *key_cache,
                     size_t workspace_bytes, int32_t *dev_status, void *stream);
 
 /*
- * 1 when mi_paged_decode needs a workspace for `num_splits` splits, else 0.
- * With 2..8 splits the splits of one (sequence, kv head) run as a thread
- * block cluster and merge through distributed shared memory, so no
- * workspace and no combine launch are needed (environment variable
- * MICROINFER_B200_CLUSTER=0 turns this off).
+ * 1 when mi_paged_decode needs a workspace for `num_splits` splits (any
+ * split count above 1), else 0.
  */
 MI_API int mi_paged_decode_uses_workspace(int32_t num_splits);
 
@@ -173,7 +180,10 @@ MI_API int mi_paged_decode_plan(int64_t num_seqs, int32_t num_q_heads,
  * position context_lens[s]-1 of sequence s (the reference's decode contract,
  * microinfer/runner.py:160-177).  Replaces the LayerKVCache.write_fast +
  * paged_attention_meta pair of CachedAttention.forward for decode
- * (microinfer/layer/cached_attention.py:76-85) with one launch.
+ * (microinfer/layer/cached_attention.py:76-85) with one launch.  The result
+ * is that of storing first and attending second, but position
+ * context_lens[s]-1 is taken from k_new/v_new directly, so no cached page
+ * waits on the store.
  *
  * flags: MI_DECODE_EARLY_KV lets the kernel read the block table, context
  * lengths and cached pages before it waits on the preceding kernel in the

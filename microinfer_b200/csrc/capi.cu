@@ -8,6 +8,7 @@
 #include "common.cuh"
 #include "launch.cuh"
 #include "params.cuh"
+#include "split_merge.cuh"
 
 namespace mi {
 
@@ -25,10 +26,14 @@ bool decode_tc_supported(int dtype, int D, int G, int block_size);
 cudaError_t launch_decode_tc(const DecodeParams &d, int dtype, int G, int64_t num_seqs,
                              int64_t num_blocks, int nsplit, cudaStream_t stream);
 cudaError_t launch_decode_fast(const DecodeParams &p, int dtype, int D, int G, int64_t num_seqs,
-                               int nsplit, cudaStream_t stream);
+                               int nsplit, bool wide, cudaStream_t stream);
+bool decode_wide_supported(int dtype, int D, int G);
 bool prefill_tc_supported(int dtype, int D, int G, int block_size);
 cudaError_t launch_prefill_tc(const AttnParams &p, int dtype, int G, int32_t max_seqlen_q,
                               bool paged, cudaStream_t stream);
+
+// Keys one 16-warp SIMT decode CTA holds in flight (16 warps x 3 stages x 8).
+constexpr int64_t kDecodeKeysPerCta = 384;
 
 static int sm_counts[64];
 static std::once_flag sm_once[64];
@@ -198,7 +203,7 @@ size_t mi_paged_decode_workspace_bytes(int64_t num_seqs, int32_t num_q_heads, in
                                        int32_t num_splits) {
   if (num_seqs <= 0 || num_q_heads <= 0 || head_dim <= 0 || num_splits <= 1) return 0;
   const size_t states = static_cast<size_t>(num_seqs) * num_q_heads * num_splits;
-  return states * (static_cast<size_t>(head_dim) + 2) * sizeof(float);
+  return kSplitCounterBytes + states * (static_cast<size_t>(head_dim) + 2) * sizeof(float);
 }
 
 int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads, int32_t max_context_hint,
@@ -206,19 +211,26 @@ int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads, int32
   if (num_seqs <= 0 || num_kv_heads <= 0) return 1;
   const int64_t sms = sm_count_of(device < 0 ? 0 : device);
   const int64_t base = num_seqs * num_kv_heads;
-  // Two decode CTAs fit per SM; stay within that single wave (a second,
-  // partial wave doubles the latency of a short decode).  With
-  // MICROINFER_B200_DECODE_CTAS_PER_SM=1 a layer fills only half the slots,
-  // leaving the other half to the next layer's early page loads.
-  static const int64_t per_sm = [] {
-    const char *v = std::getenv("MICROINFER_B200_DECODE_CTAS_PER_SM");
-    return (v != nullptr && std::strcmp(v, "1") == 0) ? 1 : 2;
-  }();
-  int64_t s = (per_sm * sms) / base;
-  if (max_context_hint > 0) {
-    const int64_t chunks = (static_cast<int64_t>(max_context_hint) + 15) / 16;
-    const int64_t cap = chunks / 8;  // keep >= 2 chunks per warp (4 warps)
-    if (s > cap) s = cap;
+  int64_t s;
+  if (2 * base <= sms) {
+    // Small batch: the layer's CTAs stay within half the SMs (one CTA per SM),
+    // so the next layer's CTAs fit beside them and request their pages while
+    // this layer runs (programmatic dependent launch); splitting further would
+    // take that room away.  Each split gets at least kDecodeKeysPerCta keys.
+    s = (sms / 2) / base;
+    if (max_context_hint > 0) {
+      const int64_t cap = (static_cast<int64_t>(max_context_hint) + kDecodeKeysPerCta - 1) /
+                          kDecodeKeysPerCta;
+      if (s > cap) s = cap;
+    }
+  } else {
+    // Larger batch: one wave of two CTAs per SM.
+    s = (2 * sms) / base;
+    if (max_context_hint > 0) {
+      const int64_t chunks = (static_cast<int64_t>(max_context_hint) + 15) / 16;
+      const int64_t cap = chunks / 8;  // keep >= 2 chunks per warp
+      if (s > cap) s = cap;
+    }
   }
   if (s < 1) s = 1;
   if (s > 256) s = 256;
@@ -227,19 +239,18 @@ int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads, int32
 
 }  // extern "C"
 
+namespace mi {
+// SIMT decode CTA shape: 16 warps (one CTA per SM) when the whole grid fits
+// one per SM, else 8 warps (two per SM).
+bool decode_simt_wide(int dtype, int D, int G, int64_t ctas, int dev) {
+  return decode_wide_supported(dtype, D, G) && ctas <= sm_count_of(dev);
+}
+}  // namespace mi
+
 namespace {
 
-bool cluster_enabled() {
-  static const bool enabled = [] {
-    const char *v = std::getenv("MICROINFER_B200_CLUSTER");
-    return !(v != nullptr && std::strcmp(v, "0") == 0);
-  }();
-  return enabled;
-}
-
-// 2..8 splits merge through a thread-block cluster (no workspace); more
-// splits (or clusters switched off) use the workspace + combine kernel.
-bool decode_uses_workspace(int nsplit) { return nsplit > 1 && !(cluster_enabled() && nsplit <= 8); }
+// Split-K merges through the workspace (last-arriver, split_merge.cuh).
+bool decode_uses_workspace(int nsplit) { return nsplit > 1; }
 
 // Decode kernels, in order of preference: tcgen05 (tensor-core, D=128 fp16 /
 // bf16, block size a multiple of 16), SIMT (bulk-copy staged, CUDA cores),
@@ -267,10 +278,14 @@ int decode_kernel_for(int dtype, int D, int G, int block_size, bool aligned, int
 
 // Split count: the caller's, else enough CTAs for one wave (the tcgen05
 // kernel holds one CTA per SM, the SIMT kernel two).
-int decode_splits_for(int kernel, int64_t num_seqs, int num_kv_heads, int num_splits, int dev) {
+int decode_splits_for(int kernel, int64_t num_seqs, int num_kv_heads, int num_splits, int dev,
+                      int64_t ctx_bound) {
   if (num_splits > 0) return num_splits;
   if (kernel == kDecodeGeneric) return 1;
-  if (kernel == kDecodeSimt) return mi_paged_decode_default_splits(num_seqs, num_kv_heads, 0, dev);
+  if (kernel == kDecodeSimt) {
+    const int64_t hint = ctx_bound > INT32_MAX ? INT32_MAX : ctx_bound;
+    return mi_paged_decode_default_splits(num_seqs, num_kv_heads, static_cast<int32_t>(hint), dev);
+  }
   const int64_t base = num_seqs * num_kv_heads;
   int64_t s = sm_count_of(dev) / base;
   if (s < 1) s = 1;
@@ -365,7 +380,8 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
     p.status = dev_status;
     return cuda_status(launch_attn_generic(p, dtype, true, st));
   }
-  const int nsplit = decode_splits_for(kernel, num_seqs, num_kv_heads, num_splits, dev);
+  const int nsplit = decode_splits_for(kernel, num_seqs, num_kv_heads, num_splits, dev,
+                                       block_table_stride * block_size);
   DecodeParams p = {};
   p.out = out;
   p.query = query;
@@ -387,17 +403,16 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
     p.new_token_stride_bytes = nt->stride * e;
   }
   if (decode_uses_workspace(nsplit)) {
+    if (num_seqs * num_kv_heads > kSplitCounters)
+      return fail(MI_ERR_UNSUPPORTED, "split-K decode takes at most 16384 (sequence, kv head) "
+                                      "pairs per launch; use num_splits=1 or smaller batches");
     const size_t need = mi_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, nsplit);
     if (workspace == nullptr || workspace_bytes < need)
       return fail(MI_ERR_INVALID, "workspace too small for num_splits (see "
                                   "mi_paged_decode_workspace_bytes)");
-    if ((reinterpret_cast<uintptr_t>(workspace) & 7u) != 0)
-      return fail(MI_ERR_ALIGNMENT, "workspace must be 8-byte aligned");
-    const size_t states = static_cast<size_t>(num_seqs) * num_q_heads * nsplit;
-    p.ws_acc = static_cast<float *>(workspace);
-    p.ws_ml = p.ws_acc + states * head_dim;
-  } else if (nsplit > 1) {
-    p.cluster_combine = 1;
+    if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0)
+      return fail(MI_ERR_ALIGNMENT, "workspace must be 16-byte aligned");
+    set_split_workspace(p, workspace, num_seqs, num_q_heads, head_dim, nsplit);
   }
   if (flags & MI_DECODE_EARLY_KV) {
     p.early_kv = 1;
@@ -406,7 +421,9 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
     const cudaError_t te = launch_decode_tc(p, dtype, G, num_seqs, num_blocks, nsplit, st);
     if (te != cudaErrorNotSupported) return cuda_status(te);
   }
-  return cuda_status(launch_decode_fast(p, dtype, head_dim, G, num_seqs, nsplit, st));
+  return cuda_status(launch_decode_fast(p, dtype, head_dim, G, num_seqs, nsplit,
+                                        decode_simt_wide(dtype, head_dim, G, num_seqs * num_kv_heads * nsplit, dev),
+                                        st));
 }
 
 }  // namespace
@@ -427,7 +444,8 @@ int mi_paged_decode_plan(int64_t num_seqs, int32_t num_q_heads, int32_t num_kv_h
     return fail(MI_ERR_INVALID, "invalid decode shape");
   const int kernel = decode_kernel_for(dtype, head_dim, num_q_heads / num_kv_heads, block_size, true,
                                        block_table_stride * block_size);
-  const int s = decode_splits_for(kernel, num_seqs, num_kv_heads, num_splits, device < 0 ? 0 : device);
+  const int s = decode_splits_for(kernel, num_seqs, num_kv_heads, num_splits, device < 0 ? 0 : device,
+                                  block_table_stride * block_size);
   if (splits_out) *splits_out = s;
   if (workspace_bytes_out)
     *workspace_bytes_out = (kernel != kDecodeGeneric && decode_uses_workspace(s))

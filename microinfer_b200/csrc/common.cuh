@@ -142,15 +142,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 
 // Bounded wait for phase `parity` of `bar`.  Returns false (and flags
 // MI_DEV_TIMEOUT) when the limit passes; callers then stop issuing work.
+// Reading %globaltimer costs far more than a try_wait round, so the clock is
+// read only after every 64 unsuccessful try_waits: a wait that succeeds soon
+// never touches it, and the limit is still enforced to within one round.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
                                                   int32_t *status) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t start = global_ns();
+  uint64_t start = 0;
   for (;;) {
 #pragma unroll 1
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
-    if (global_ns() - start > kWaitLimitNs) {
+    const uint64_t now = global_ns();
+    if (start == 0) {
+      start = now;
+    } else if (now - start > kWaitLimitNs) {
       flag_status(status, MI_DEV_TIMEOUT);
       return false;
     }
@@ -166,6 +171,11 @@ __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src_gmem, u
           smem_addr(dst_smem)),
       "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
+}
+
+// Bulk prefetch of `bytes` (a multiple of 16, 16-byte aligned) into L2.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 // Programmatic dependent launch controls (no-ops when launched without PDL).

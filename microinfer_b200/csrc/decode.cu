@@ -1,11 +1,11 @@
 // HBM-bound paged decode attention for sm_100a.
 //
 // paged_decode_kernel: one CTA per (split, kv head, sequence), so each K/V
-// byte is read once for the whole GQA group.  Four warps each stream their
-// own 16-key chunks (chunk ids strided over splits and warps, so a CTA knows
+// byte is read once for the whole GQA group.  Eight warps each stream their
+// own 8-key chunks (chunk ids strided over splits and warps, so a CTA knows
 // them before the context length arrives) through a ring of shared-memory
 // stages filled by cp.async.bulk row copies -- one row per lane, K rows on
-// lanes 0-15 and V rows on 16-31 -- completing on an mbarrier.  The context
+// lanes 0-7 and V rows on 8-15 -- completing on an mbarrier.  The context
 // length, the block-table entries of the first stages and the slot of this
 // step's token are fetched in a single round trip.
 //
@@ -14,31 +14,30 @@
 // each lane whole dot products; the online softmax rescales lazily (only when
 // a score passes the running max by 2^8).  p.V accumulates in fp32x2 pairs.
 //
-// Optional fused store_kvcache: the warp that owns the chunk holding this
-// step's token writes k_new/v_new into its slot, fences the async proxy and
-// only then bulk-copies that chunk, so the attention sees the new token
-// without a separate store launch.
+// Optional fused store_kvcache: this step's token (position ctx-1) is not
+// read back from the pool.  Its k_new/v_new rows are loaded into registers by
+// one warp, folded into that warp's softmax state after its chunks, and
+// written to the token's slot; every cached page can therefore be requested
+// before the preceding kernel finishes (early_kv), and nothing waits on the
+// store.
 //
-// Split-K: with 2..8 splits the splits of one (seq, kv head) run as a thread
-// block cluster and rank 0 merges their (m, l, acc) states through
-// distributed shared memory; with more splits the states go to a workspace
-// and decode_combine_kernel merges them.
-#include <cooperative_groups.h>
+// Split-K: the splits of one (seq, kv head) store their (m, l, acc) states
+// in the workspace and the last one to finish merges them (split_merge.cuh).
 #include <float.h>
 
 #include "common.cuh"
 #include "launch.cuh"
 #include "params.cuh"
-
-namespace cg = cooperative_groups;
+#include "split_merge.cuh"
 
 namespace mi {
 
 namespace {
 constexpr unsigned kFull = 0xffffffffu;
+constexpr int kL2Ahead = 4;  // chunks per warp prefetched into L2 beyond the smem ring
 }
 
-template <typename T, int D, int G>
+template <typename T, int D, int G, int W>
 struct DecCfg {
   static constexpr int kRowBytes = D * static_cast<int>(sizeof(T));
   static constexpr int kVec = 16 / static_cast<int>(sizeof(T));  // elements per 16 B
@@ -56,16 +55,17 @@ struct DecCfg {
   static constexpr int kDup = kV0 >= kLPR ? 1 : kLPR / kV0;  // lanes holding the same dot
   static constexpr int kStageBytes = kKeys * 2 * kRowBytes;
   static constexpr int kStages = kStageBytes <= 4096 ? 3 : 2;
-  static constexpr int kWarps = 8;
+  static constexpr int kWarps = W;
   static constexpr int kThreads = kWarps * 32;
   static constexpr int kSmemStages = kWarps * kStages * kStageBytes;
   static constexpr int kSmemP = kWarps * kKeys * G * 4;
   static constexpr int kSmemBars = kWarps * kStages * 8;
   static constexpr int kSmemMerge = kWarps * G * (D + 2) * 4;
-  static constexpr int kSmemFin = G * (D + 2) * 4;
-  static constexpr int kSmem = kSmemStages + kSmemP + kSmemBars;
-  static constexpr int kNewLanes = (2 * kChunks + 31) / 32;  // 16 B pieces per lane for the store
-  static_assert(kSmemMerge + kSmemFin <= kSmemStages, "merge buffers alias the stage ring");
+  static constexpr int kSmem = kSmemStages + kSmemP + kSmemBars + 16;
+  // 16 warps (one CTA per SM, 384 keys in flight) where 3 stages fit and the
+  // group's registers stay within 128 per thread
+  static constexpr bool kWideOk = kStageBytes <= 4096 && G <= 4;
+  static_assert(kSmemMerge <= kSmemStages, "merge buffers alias the stage ring");
   static_assert(kRPS <= kKeys, "row too short for the lane mapping");
   static_assert(kKPG % kSub == 0, "sub-step must divide the group's keys");
 };
@@ -97,13 +97,14 @@ __device__ __forceinline__ void transpose_reduce(float (&v)[N], int c) {
   }
 }
 
-template <typename T, int D, int G>
-__global__ void __launch_bounds__(256, G >= 8 ? 1 : 2) paged_decode_kernel(DecodeParams p) {
-  using C = DecCfg<T, D, G>;
+template <typename T, int D, int G, int W>
+__global__ void __launch_bounds__(W * 32, (W == 8 && G < 8) ? 2 : 1) paged_decode_kernel(DecodeParams p) {
+  using C = DecCfg<T, D, G, W>;
   extern __shared__ __align__(128) char smem[];
   char *stage_mem = smem;
   float *p_smem = reinterpret_cast<float *>(smem + C::kSmemStages);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kSmemStages + C::kSmemP);
+  int *last_flag = reinterpret_cast<int *>(bars + C::kWarps * C::kStages);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, nsplit = gridDim.x;
@@ -146,13 +147,15 @@ __global__ void __launch_bounds__(256, G >= 8 ? 1 : 2) paged_decode_kernel(Decod
     if (threadIdx.x == 0 && split == 0) flag_status(p.status, MI_DEV_BAD_BLOCK);
     ctx = static_cast<int>(cap);
   }
-  const int nchunks = ctx > 0 ? (ctx + C::kKeys - 1) / C::kKeys : 0;
+  // With the fused store, position ctx-1 is this step's token: it comes from
+  // k_new/v_new (folded in by warp 0 of one split), not from the pool.
+  const bool fold = fused && slot >= 0 && ctx > 0;
+  const int ctx_kv = fold ? ctx - 1 : ctx;  // keys read from the pool
+  const bool own_new = fold && warp == 0 && split == ((ctx - 1) / C::kKeys) % nsplit;
+  const int nchunks = ctx_kv > 0 ? (ctx_kv + C::kKeys - 1) / C::kKeys : 0;
   const int first = split + nsplit * warp;
   const int stride = nsplit * C::kWarps;
   const int my_n = first < nchunks ? (nchunks - first + stride - 1) / stride : 0;
-  const int last_chunk = nchunks - 1;
-  const bool own_last = fused && slot >= 0 && last_chunk >= 0 && last_chunk % nsplit == split &&
-                        (last_chunk / nsplit) % C::kWarps == warp;
 
   const int64_t tok_bytes = static_cast<int64_t>(p.num_kv_heads) * C::kRowBytes;
   const char *kv_src_base = (copy_kind ? p.value_cache : p.key_cache) +
@@ -161,37 +164,14 @@ __global__ void __launch_bounds__(256, G >= 8 ? 1 : 2) paged_decode_kernel(Decod
   // Validate a prefetched table entry for this lane's row of chunk ci.
   auto check_blk = [&](int ci, int64_t blk) -> int64_t {
     const int key = ci * C::kKeys + copy_key;
-    if (!copy_lane || key >= ctx) return -1;
+    if (!copy_lane || key >= ctx_kv) return -1;
     if (blk < 0 || blk >= p.num_blocks) {
       flag_status(p.status, MI_DEV_BAD_BLOCK);
       return -1;
     }
     return blk;
   };
-  // Fused store of this step's token (head kvh) before its chunk is copied.
-  auto store_new_token = [&]() {
-    if (slot >= p.num_blocks * p.block_size) {
-      if (lane == 0) flag_status(p.status, MI_DEV_BAD_SLOT);
-      return;
-    }
-#pragma unroll
-    for (int i = 0; i < C::kNewLanes; ++i) {
-      const int piece = lane + 32 * i;
-      if (piece < 2 * C::kChunks) {
-        const int kind = piece / C::kChunks, chunk = piece % C::kChunks;
-        const char *src = (kind ? p.v_new : p.k_new) + seq * p.new_token_stride_bytes +
-                          static_cast<int64_t>(kvh) * C::kRowBytes + chunk * 16;
-        char *dst = const_cast<char *>(kind ? p.value_cache : p.key_cache) +
-                    (slot * p.num_kv_heads + kvh) * C::kRowBytes + chunk * 16;
-        *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
-      }
-    }
-    // Order the generic-proxy stores before the bulk copy (async proxy) below.
-    asm volatile("fence.proxy.async.global;" ::: "memory");
-    __syncwarp();
-  };
   auto issue = [&](int ci, int st, int64_t blk) {
-    if (own_last && ci == last_chunk) store_new_token();
     const int key = ci * C::kKeys + copy_key;
     const bool go = blk >= 0;
     const unsigned mask = __ballot_sync(kFull, go);
@@ -205,30 +185,41 @@ __global__ void __launch_bounds__(256, G >= 8 ? 1 : 2) paged_decode_kernel(Decod
   };
 
   // Prologue: fill the ring.  With early_kv the cached pages are requested
-  // before waiting on the preceding kernel; the chunk that receives this
-  // step's token (whose K/V that kernel may have produced) waits for it.
+  // before waiting on the preceding kernel.
   int issued = 0;
-  int deferred = -1;
-  int64_t deferred_blk = -1;
 #pragma unroll
   for (int s = 0; s < C::kStages; ++s) {
     if (s < my_n) {
       const int ci = chunk_of(s);
-      if (p.early_kv && own_last && ci == last_chunk) {
-        deferred = s;
-        deferred_blk = pre_blk[s];
-      } else {
-        issue(ci, s, check_blk(ci, pre_blk[s]));
-      }
+      issue(ci, s, check_blk(ci, pre_blk[s]));
       ++issued;
     }
+  }
+  // Chunks beyond the ring: warm L2 with their rows now, so their copies come
+  // from L2 once the ring drains (bad ids are only skipped here; the copy
+  // itself flags them).
+#pragma unroll 1
+  for (int it = C::kStages; it < my_n && it < C::kStages + kL2Ahead; ++it) {
+    const int ci = chunk_of(it);
+    const int key = ci * C::kKeys + copy_key;
+    const int64_t blk = table_entry(ci);
+    if (copy_lane && key < ctx_kv && blk >= 0 && blk < p.num_blocks)
+      prefetch_l2_bulk(kv_src_base + (blk * p.block_size + key % p.block_size) * tok_bytes,
+                       C::kRowBytes);
   }
   if (p.early_kv) {
     pdl_launch_dependents();  // the next kernel may start its own prologue
     pdl_wait();
-    if (deferred >= 0) {
-      const int ci = chunk_of(deferred);
-      issue(ci, deferred, check_blk(ci, deferred_blk));
+  }
+  // This step's token: this lane's 16-byte pieces of the K and V rows (lane
+  // group r holds the same dimensions as its q and acc registers).
+  uint4 knew[C::kCPL], vnew[C::kCPL];
+  if (own_new) {
+    const int64_t off = seq * p.new_token_stride_bytes + static_cast<int64_t>(kvh) * C::kRowBytes;
+#pragma unroll
+    for (int cp = 0; cp < C::kCPL; ++cp) {
+      knew[cp] = *reinterpret_cast<const uint4 *>(p.k_new + off + (cp * C::kLPR + c) * 16);
+      vnew[cp] = *reinterpret_cast<const uint4 *>(p.v_new + off + (cp * C::kLPR + c) * 16);
     }
   }
 
@@ -295,7 +286,7 @@ __global__ void __launch_bounds__(256, G >= 8 ? 1 : 2) paged_decode_kernel(Decod
     consumed = it + 1;
     const char *kst = wstage + st * C::kStageBytes;
     const char *vst = kst + C::kKeys * C::kRowBytes;
-    const int valid = ctx - ci * C::kKeys;  // keys of this chunk below ctx (>= 1)
+    const int valid = ctx_kv - ci * C::kKeys;  // keys of this chunk read from the pool (>= 1)
 
     // ---- scores: q . k for the group's keys ----
     float sc[C::kNSub][C::kF];
@@ -417,6 +408,60 @@ __global__ void __launch_bounds__(256, G >= 8 ? 1 : 2) paged_decode_kernel(Decod
 #pragma unroll
     for (int h = 0; h < G; ++h) m_run[h] = -INFINITY;
   }
+
+  // ---- this step's token: fold into the warp's state, write it to its slot ----
+  float l_new[G];
+#pragma unroll
+  for (int h = 0; h < G; ++h) l_new[h] = 0.f;
+  if (own_new) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float2 part = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int cp = 0; cp < C::kCPL; ++cp) {
+        float2 f[C::kVec / 2];
+        Vec16<T>::unpack(knew[cp], f);
+#pragma unroll
+        for (int e = 0; e < C::kVec / 2; ++e) part = ffma2(f[e], q2[h][cp * C::kVec / 2 + e], part);
+      }
+      float s = part.x + part.y;
+#pragma unroll
+      for (int m = C::kLPR / 2; m >= 1; m >>= 1) s += __shfl_xor_sync(kFull, s, m);
+      const float m_new = fmaxf(m_run[h], s);
+      const float alpha = m_run[h] == -INFINITY ? 0.f : fast_exp2(m_run[h] - m_new);
+      const float pn = fast_exp2(s - m_new);
+      const float2 a2 = make_float2(alpha, alpha);
+#pragma unroll
+      for (int cp = 0; cp < C::kCPL; ++cp) {
+        float2 f[C::kVec / 2];
+        Vec16<T>::unpack(vnew[cp], f);
+#pragma unroll
+        for (int e = 0; e < C::kVec / 2; ++e) {
+          float2 &a = acc2[h][cp * C::kVec / 2 + e];
+          a = fmul2(a, a2);
+          // lane groups are summed below: only group 0 adds the token
+          if (r == 0) a = ffma2(f[e], make_float2(pn, pn), a);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < C::kF; ++j)
+        if (slot_head[j] == h) l_part[j] *= alpha;
+      m_run[h] = m_new;
+      l_new[h] = pn;
+    }
+    if (slot < p.num_blocks * p.block_size) {
+      if (r == 0) {
+        const int64_t row = (slot * p.num_kv_heads + kvh) * C::kRowBytes;
+#pragma unroll
+        for (int cp = 0; cp < C::kCPL; ++cp) {
+          *reinterpret_cast<uint4 *>(const_cast<char *>(p.key_cache) + row + (cp * C::kLPR + c) * 16) = knew[cp];
+          *reinterpret_cast<uint4 *>(const_cast<char *>(p.value_cache) + row + (cp * C::kLPR + c) * 16) = vnew[cp];
+        }
+      }
+    } else if (lane == 0) {
+      flag_status(p.status, MI_DEV_BAD_SLOT);
+    }
+  }
   pdl_launch_dependents();
 
   // ---- merge lane groups inside the warp (they share m_run) ----
@@ -438,15 +483,13 @@ __global__ void __launch_bounds__(256, G >= 8 ? 1 : 2) paged_decode_kernel(Decod
       if (slot_owner[j] && slot_head[j] == h) x += l_part[j];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(kFull, x, o);
-    l_head[h] = x;
+    l_head[h] = x + l_new[h];
   }
 
   // ---- merge the warps through shared memory (aliases the drained ring) ----
   __syncthreads();
   float *mg_acc = reinterpret_cast<float *>(stage_mem);  // [warps][G][D]
   float *mg_ml = mg_acc + C::kWarps * G * D;              // [warps][G][2]
-  float *fin_acc = mg_ml + C::kWarps * G * 2;             // [G][D]   (cluster merge)
-  float *fin_ml = fin_acc + G * D;                        // [G][2]
   if (r == 0) {
 #pragma unroll
     for (int h = 0; h < G; ++h)
@@ -466,7 +509,6 @@ __global__ void __launch_bounds__(256, G >= 8 ? 1 : 2) paged_decode_kernel(Decod
     }
   }
   __syncthreads();
-  const bool cluster_merge = p.cluster_combine != 0 && nsplit > 1;
   for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
     const int h = i / D, d = i % D;
     float M = -INFINITY;
@@ -484,91 +526,18 @@ __global__ void __launch_bounds__(256, G >= 8 ? 1 : 2) paged_decode_kernel(Decod
     if (nsplit == 1) {
       T *o = static_cast<T *>(p.out) + (seq * p.num_q_heads + qh) * D;
       o[d] = Elem<T>::from_float(L > 0.f ? A / L : 0.f);
-    } else if (cluster_merge) {
-      fin_acc[h * D + d] = A;
-      if (d == 0) {
-        fin_ml[h * 2] = M;
-        fin_ml[h * 2 + 1] = L;
-      }
     } else {
-      const int64_t state = (seq * p.num_q_heads + qh) * nsplit + split;
-      p.ws_acc[state * D + d] = A;
-      if (d == 0) {
-        p.ws_ml[state * 2] = M;
-        p.ws_ml[state * 2 + 1] = L;
-      }
+      split_store_state(p, seq, qh, nsplit, split, D, d, M, L, A);
     }
   }
-  if (cluster_merge) {
-    // The splits of this (seq, kv head) are the CTAs of one cluster along x.
-    // Each rank finalises a slice of the (head, dim) outputs, issuing all of
-    // its remote (DSMEM) loads before using any of them.
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    for (int i = split * C::kThreads + threadIdx.x; i < G * D; i += nsplit * C::kThreads) {
-      const int h = i / D, d = i % D;
-      float ms[8], ls[8], as[8];
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        if (s < nsplit) {
-          const float *rml = cluster.map_shared_rank(fin_ml, s);
-          ms[s] = rml[h * 2];
-          ls[s] = rml[h * 2 + 1];
-          as[s] = cluster.map_shared_rank(fin_acc, s)[h * D + d];
-        }
-      }
-      float M = -INFINITY;
-#pragma unroll
-      for (int s = 0; s < 8; ++s)
-        if (s < nsplit) M = fmaxf(M, ms[s]);
-      float L = 0.f, A = 0.f;
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        if (s < nsplit) {
-          const float f = (ms[s] == -INFINITY) ? 0.f : fast_exp2(ms[s] - M);
-          L += f * ls[s];
-          A += f * as[s];
-        }
-      }
-      T *o = static_cast<T *>(p.out) + (seq * p.num_q_heads + kvh * G + h) * D;
-      o[d] = Elem<T>::from_float(L > 0.f ? A / L : 0.f);
-    }
-    cluster.sync();  // keep every rank's shared memory alive until all reads are done
-  }
+  if (nsplit > 1) split_arrive_and_merge<T, G, D>(p, seq, kvh, nsplit, last_flag);
 }
 
-// Merge split-K states: grid (Hq, N), one thread per output element.
-template <typename T>
-__global__ void __launch_bounds__(128) decode_combine_kernel(DecodeParams p, int nsplit, int D) {
-  pdl_wait();
-  const int qh = blockIdx.x;
-  const int64_t seq = blockIdx.y;
-  const int64_t state0 = (seq * p.num_q_heads + qh) * nsplit;
-  float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, p.ws_ml[(state0 + s) * 2]);
-  float L = 0.f;
-  for (int s = 0; s < nsplit; ++s) {
-    const float ms = p.ws_ml[(state0 + s) * 2];
-    if (ms != -INFINITY) L += fast_exp2(ms - M) * p.ws_ml[(state0 + s) * 2 + 1];
-  }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  T *o = static_cast<T *>(p.out) + (seq * p.num_q_heads + qh) * D;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float A = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float ms = p.ws_ml[(state0 + s) * 2];
-      if (ms != -INFINITY) A += fast_exp2(ms - M) * p.ws_acc[(state0 + s) * D + d];
-    }
-    o[d] = Elem<T>::from_float(A * inv);
-  }
-  pdl_launch_dependents();
-}
-
-template <typename T, int D, int G>
-static cudaError_t launch_decode_tdg(const DecodeParams &p, int64_t num_seqs, int nsplit,
-                                     cudaStream_t stream) {
-  using C = DecCfg<T, D, G>;
-  auto kern = paged_decode_kernel<T, D, G>;
+template <typename T, int D, int G, int W>
+static cudaError_t launch_decode_tdgw(const DecodeParams &p, int64_t num_seqs, int nsplit,
+                                      cudaStream_t stream) {
+  using C = DecCfg<T, D, G, W>;
+  auto kern = paged_decode_kernel<T, D, G, W>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -578,48 +547,28 @@ static cudaError_t launch_decode_tdg(const DecodeParams &p, int64_t num_seqs, in
     attr_set[dev] = true;
   }
   const dim3 grid(nsplit, p.num_kv_heads, static_cast<unsigned>(num_seqs));
-  if (p.cluster_combine && nsplit > 1) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = dim3(C::kThreads);
-    cfg.dynamicSmemBytes = C::kSmem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = nsplit;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, kern, p);
+  return launch_pdl(kern, grid, dim3(C::kThreads), C::kSmem, stream, p);
+}
+
+template <typename T, int D, int G>
+static cudaError_t launch_decode_tdg(const DecodeParams &p, int64_t num_seqs, int nsplit, bool wide,
+                                     cudaStream_t stream) {
+  if constexpr (DecCfg<T, D, G, 16>::kWideOk) {
+    if (wide) return launch_decode_tdgw<T, D, G, 16>(p, num_seqs, nsplit, stream);
   }
-  cudaError_t e = launch_pdl(kern, grid, dim3(C::kThreads), C::kSmem, stream, p);
-  if (e != cudaSuccess || nsplit == 1) return e;
-  return launch_pdl(decode_combine_kernel<T>, dim3(p.num_q_heads, static_cast<unsigned>(num_seqs)),
-                    dim3(128), 0, stream, p, nsplit, D);
+  return launch_decode_tdgw<T, D, G, 8>(p, num_seqs, nsplit, stream);
 }
 
 template <typename T, int D>
-static cudaError_t launch_decode_td(const DecodeParams &p, int G, int64_t n, int s, cudaStream_t st) {
+static cudaError_t launch_decode_td(const DecodeParams &p, int G, int64_t n, int s, bool wide,
+                                    cudaStream_t st) {
   switch (G) {
-    case 1: return launch_decode_tdg<T, D, 1>(p, n, s, st);
-    case 2: return launch_decode_tdg<T, D, 2>(p, n, s, st);
-    case 4: return launch_decode_tdg<T, D, 4>(p, n, s, st);
-    case 8: return launch_decode_tdg<T, D, 8>(p, n, s, st);
+    case 1: return launch_decode_tdg<T, D, 1>(p, n, s, wide, st);
+    case 2: return launch_decode_tdg<T, D, 2>(p, n, s, wide, st);
+    case 4: return launch_decode_tdg<T, D, 4>(p, n, s, wide, st);
+    case 8: return launch_decode_tdg<T, D, 8>(p, n, s, wide, st);
   }
   return cudaErrorInvalidValue;
-}
-
-cudaError_t launch_decode_combine(const DecodeParams &p, int dtype, int D, int64_t num_seqs,
-                                  int nsplit, cudaStream_t stream) {
-  const dim3 grid(p.num_q_heads, static_cast<unsigned>(num_seqs));
-  if (dtype == MI_DTYPE_FLOAT32)
-    return launch_pdl(decode_combine_kernel<float>, grid, dim3(128), 0, stream, p, nsplit, D);
-  if (dtype == MI_DTYPE_FLOAT16)
-    return launch_pdl(decode_combine_kernel<__half>, grid, dim3(128), 0, stream, p, nsplit, D);
-  return launch_pdl(decode_combine_kernel<__nv_bfloat16>, grid, dim3(128), 0, stream, p, nsplit, D);
 }
 
 bool decode_fast_supported(int dtype, int D, int G) {
@@ -628,20 +577,26 @@ bool decode_fast_supported(int dtype, int D, int G) {
   return D == 64 || D == 128 || D == 256;
 }
 
+// 16-warp variant available: 3 stages of 8 rows fit (2-byte elements with
+// D <= 128, or fp32 with D = 64) and the GQA group is at most 4.
+bool decode_wide_supported(int dtype, int D, int G) {
+  return G <= 4 && (dtype == MI_DTYPE_FLOAT32 ? D == 64 : D <= 128);
+}
+
 cudaError_t launch_decode_fast(const DecodeParams &p, int dtype, int D, int G, int64_t num_seqs,
-                               int nsplit, cudaStream_t stream) {
+                               int nsplit, bool wide, cudaStream_t stream) {
   if (dtype == MI_DTYPE_FLOAT32) {
-    if (D == 64) return launch_decode_td<float, 64>(p, G, num_seqs, nsplit, stream);
-    return launch_decode_td<float, 128>(p, G, num_seqs, nsplit, stream);
+    if (D == 64) return launch_decode_td<float, 64>(p, G, num_seqs, nsplit, wide, stream);
+    return launch_decode_td<float, 128>(p, G, num_seqs, nsplit, wide, stream);
   }
   if (dtype == MI_DTYPE_FLOAT16) {
-    if (D == 64) return launch_decode_td<__half, 64>(p, G, num_seqs, nsplit, stream);
-    if (D == 128) return launch_decode_td<__half, 128>(p, G, num_seqs, nsplit, stream);
-    return launch_decode_td<__half, 256>(p, G, num_seqs, nsplit, stream);
+    if (D == 64) return launch_decode_td<__half, 64>(p, G, num_seqs, nsplit, wide, stream);
+    if (D == 128) return launch_decode_td<__half, 128>(p, G, num_seqs, nsplit, wide, stream);
+    return launch_decode_td<__half, 256>(p, G, num_seqs, nsplit, wide, stream);
   }
-  if (D == 64) return launch_decode_td<__nv_bfloat16, 64>(p, G, num_seqs, nsplit, stream);
-  if (D == 128) return launch_decode_td<__nv_bfloat16, 128>(p, G, num_seqs, nsplit, stream);
-  return launch_decode_td<__nv_bfloat16, 256>(p, G, num_seqs, nsplit, stream);
+  if (D == 64) return launch_decode_td<__nv_bfloat16, 64>(p, G, num_seqs, nsplit, wide, stream);
+  if (D == 128) return launch_decode_td<__nv_bfloat16, 128>(p, G, num_seqs, nsplit, wide, stream);
+  return launch_decode_td<__nv_bfloat16, 256>(p, G, num_seqs, nsplit, wide, stream);
 }
 
 }  // namespace mi

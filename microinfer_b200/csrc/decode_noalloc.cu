@@ -14,9 +14,10 @@
 // code cannot use the array's name as a device address, so on the first call
 // on each device (with that device current) its address is looked up once
 // with cudaGetSymbolAddress and cached; make that first call outside any
-// stream capture.  All calls share the one array and it keeps the previous
-// call's contents: the kernels write every split state before the combine
-// reads it, so nothing needs clearing, but calls that overlap on the GPU (two
+// stream capture.  All calls share the one array.  It starts zeroed (static
+// storage), the split-K arrival counters at its start are left at zero by
+// every launch, and every split state is written before it is read, so
+// nothing needs clearing between calls; calls that overlap on the GPU (two
 // streams, or two threads) race on the array and must be serialised by the
 // caller.
 #include <mutex>
@@ -24,6 +25,7 @@
 #include "common.cuh"
 #include "launch.cuh"
 #include "params.cuh"
+#include "split_merge.cuh"
 
 namespace mi {
 
@@ -31,7 +33,8 @@ int capi_fail(int code, const char *msg);
 int capi_select_device(const void *p);
 bool decode_fast_supported(int dtype, int D, int G);
 cudaError_t launch_decode_fast(const DecodeParams &p, int dtype, int D, int G, int64_t num_seqs,
-                               int nsplit, cudaStream_t stream);
+                               int nsplit, bool wide, cudaStream_t stream);
+bool decode_simt_wide(int dtype, int D, int G, int64_t ctas, int dev);
 cudaError_t launch_attn_generic(const AttnParams &p, int dtype, bool paged, cudaStream_t stream);
 
 constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;
@@ -124,8 +127,12 @@ extern "C" int mi_paged_decode_noalloc(void *out, const void *query, const void 
 
   int dev = 0;
   cudaGetDevice(&dev);
+  const int64_t ctx_bound = block_table_stride * block_size;
   const int nsplit =
-      num_splits == 0 ? mi_paged_decode_default_splits(num_seqs, num_kv_heads, 0, dev) : num_splits;
+      num_splits == 0 ? mi_paged_decode_default_splits(
+                            num_seqs, num_kv_heads,
+                            static_cast<int32_t>(ctx_bound > INT32_MAX ? INT32_MAX : ctx_bound), dev)
+                      : num_splits;
   DecodeParams p = {};
   p.out = out;
   p.query = query;
@@ -141,18 +148,22 @@ extern "C" int mi_paged_decode_noalloc(void *out, const void *query, const void 
   p.scale_log2 = scale_log2;
   p.status = dev_status;
   if (nsplit > 1) {
+    if (num_seqs * num_kv_heads > kSplitCounters)
+      return capi_fail(MI_ERR_UNSUPPORTED, "split-K decode takes at most 16384 (sequence, kv "
+                                           "head) pairs per launch; use num_splits=1");
     const size_t need = mi_paged_decode_workspace_bytes(num_seqs, num_q_heads, head_dim, nsplit);
     if (need > kNoAllocScratchBytes)
       return capi_fail(MI_ERR_INVALID,
                        "split-K state exceeds the 2 MiB built-in scratch of "
-                       "mi_paged_decode_noalloc (num_seqs * num_q_heads * num_splits * "
-                       "(head_dim + 2) * 4 bytes); use fewer splits or mi_paged_decode");
+                       "mi_paged_decode_noalloc (64 KiB + num_seqs * num_q_heads * "
+                       "num_splits * (head_dim + 2) * 4 bytes); use fewer splits or "
+                       "mi_paged_decode");
     float *scratch = nullptr;
     if (const int s = scratch_address(&scratch)) return s;
-    const size_t states = static_cast<size_t>(num_seqs) * num_q_heads * nsplit;
-    p.ws_acc = scratch;
-    p.ws_ml = scratch + states * head_dim;
+    set_split_workspace(p, scratch, num_seqs, num_q_heads, head_dim, nsplit);
   }
-  const cudaError_t e = launch_decode_fast(p, dtype, head_dim, G, num_seqs, nsplit, st);
+  const cudaError_t e =
+      launch_decode_fast(p, dtype, head_dim, G, num_seqs, nsplit,
+                         decode_simt_wide(dtype, head_dim, G, num_seqs * num_kv_heads * nsplit, dev), st);
   return e == cudaSuccess ? MI_OK : capi_fail(static_cast<int>(e), cudaGetErrorString(e));
 }

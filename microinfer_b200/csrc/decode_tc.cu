@@ -12,8 +12,7 @@
 // 224 threads:
 //   warp 0    K producer: TMA of 8 groups of 16 keys per tile (3-D map over
 //             [slots, Hkv, D], slot from the block table, zero fill past the
-//             context) into a 3-stage ring; the G query rows; the fused store
-//             of this step's token.
+//             context) into a 3-stage ring; the G query rows.
 //   warp 6    V producer: the same for V, so K runs ahead of V (K frees after
 //             the S MMA, V only after P.V).
 //   warp 1    TMEM owner (64 columns) and single-thread MMA issuer, issuing
@@ -23,10 +22,13 @@
 //             of O^T (only when a head's max grows by more than 2^8), P^T
 //             (double-buffered) written as the B operand of the next MMA;
 //             epilogue with one head dimension per thread.
-// Splits merge through a thread-block cluster (2..8) or a workspace.  Every
-// wait is bounded; the softmax warps abort together (barrier.red.or), so no
-// warp is ever left at a barrier.
-#include <cooperative_groups.h>
+// With the fused store, this step's token (position ctx-1) is not read from
+// the pool: the softmax warps of one split load its k_new/v_new rows, fold it
+// into the final state and write it to its slot, so every cached tile can be
+// requested before the preceding kernel finishes (early_kv).
+// Splits store their states and the last one to finish merges them
+// (split_merge.cuh).  Every wait is bounded; the softmax warps abort
+// together (barrier.red.or), so no warp is ever left at a barrier.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -35,9 +37,8 @@
 #include "common.cuh"
 #include "launch.cuh"
 #include "params.cuh"
+#include "split_merge.cuh"
 #include "tc_helpers.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace mi {
 
@@ -77,8 +78,7 @@ enum {
   B_PFULL = 17,   // +P buffer (2)
   B_ODONE = 19,   // +P buffer: P.V of tiles with that parity done
   B_FIN = 21,
-  B_STORED = 22,  // the fused store of this step's token is visible
-  B_COUNT = 23
+  B_COUNT = 22
 };
 
 __device__ __forceinline__ uint64_t k_desc(uint32_t tile, int kk) {  // K tile, K-major
@@ -166,7 +166,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&bar[B_ODONE + b], 1);
     }
     mbar_init(&bar[B_FIN], 1);
-    mbar_init(&bar[B_STORED], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -185,11 +184,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0 && split == 0) flag_status(p.status, MI_DEV_BAD_BLOCK);
     ctx = static_cast<int>(cap);
   }
-  const int ntiles = ctx > 0 ? (ctx + 127) / 128 : 0;
-  const int my_n = split < ntiles ? (ntiles - split + nsplit - 1) / nsplit : 0;
-  const int last_tile = ntiles - 1;
   const int64_t slot = p.k_new != nullptr ? static_cast<int64_t>(p.slot_mapping[seq]) : -1;
-  const bool own_last = slot >= 0 && last_tile >= 0 && last_tile % nsplit == split;
+  // With the fused store, position ctx-1 is this step's token, folded in from
+  // k_new/v_new by one split instead of being read back from the pool.
+  const bool fold = slot >= 0 && ctx > 0;
+  const int ctx_kv = fold ? ctx - 1 : ctx;  // keys read from the pool
+  const bool own_new = fold && split == ((ctx - 1) / 128) % nsplit;
+  const int ntiles = ctx_kv > 0 ? (ctx_kv + 127) / 128 : 0;
+  const int my_n = split < ntiles ? (ntiles - split + nsplit - 1) / nsplit : 0;
   auto tile_of = [&](int it) { return split + nsplit * it; };
 
   if (warp == 0 || warp == 6) {
@@ -204,7 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     auto row_of = [&](int it) -> int {
       if (lane >= 16 || it >= my_n) return 0;
       const int key0 = tile_of(it) * 128 + g * 16;
-      if (key0 >= ctx) return static_cast<int>(P.kv_rows);  // zero fill
+      if (key0 >= ctx_kv) return static_cast<int>(P.kv_rows);  // zero fill
       const int64_t col = key0 / p.block_size;
       const int64_t blk = col < p.bt_stride ? table[col] : -1;
       if (blk < 0 || blk >= p.num_blocks) {
@@ -226,56 +228,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc::tma_load_3d(ring + s * kTile + dh * kHalf + g * 2048, map, dh * 64, kvh, row, &full_b[s]);
       return true;
     };
-    // This step's token (head kvh) goes to the pool before its tile is copied.
-    auto store_token = [&]() {
-      if (slot < p.num_blocks * p.block_size) {
-        const int kind = lane >> 4, chunk = lane & 15;  // 2 x 16 pieces of 16 bytes
-        const char *src = (kind ? p.v_new : p.k_new) + seq * p.new_token_stride_bytes +
-                          static_cast<int64_t>(kvh) * 256 + chunk * 16;
-        char *dst = const_cast<char *>(kind ? p.value_cache : p.key_cache) +
-                    (slot * p.num_kv_heads + kvh) * 256 + chunk * 16;
-        *reinterpret_cast<uint4 *>(dst) = *reinterpret_cast<const uint4 *>(src);
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-      } else if (lane == 0) {
-        flag_status(p.status, MI_DEV_BAD_SLOT);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar[B_STORED]);
-    };
-    // Before loading the new token's tile: K producer stores it, V producer
-    // waits until the store is visible.
-    auto before_new_tile = [&]() -> bool {
-      if (!is_v) {
-        store_token();
-        return true;
-      }
-      int good = 1;
-      if (lane == 0) good = mbar_wait_bounded(&bar[B_STORED], 0, p.status);
-      return __shfl_sync(kFull, good, 0) != 0;
-    };
     if (lane == 0) tc::prefetch_tmap(map);
     bool ok = true;
-    int deferred = -1;
     int row = row_of(0);
     int it = 0;
     for (; it < kStages && it < my_n && ok; ++it) {
       const int next_row = row_of(it + 1);
-      const bool new_tile = own_last && tile_of(it) == last_tile;
-      if (new_tile && p.early_kv) {
-        deferred = it;
-      } else {
-        if (new_tile) ok = before_new_tile();
-        if (ok) ok = load(it, row);
-      }
+      ok = load(it, row);
       row = next_row;
     }
     if (p.early_kv) {
       if (!is_v) pdl_launch_dependents();
       pdl_wait();
-      if (deferred >= 0 && ok) {
-        ok = before_new_tile();
-        if (ok) ok = load(deferred, row_of(deferred));
-      }
     }
     if (!is_v && lane == 0) {
       mbar_arrive_expect_tx(&bar[B_Q], 2 * G * 128);
@@ -285,8 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (; it < my_n && ok; ++it) {
       const int next_row = row_of(it + 1);  // table lookup of the next tile overlaps the wait
-      if (own_last && tile_of(it) == last_tile) ok = before_new_tile();
-      if (ok) ok = load(it, row);
+      ok = load(it, row);
       row = next_row;
     }
     if (!ok && lane == 0) *(volatile int *)abort_flag = 1;
@@ -299,10 +262,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
+    // Polls (test_wait) for whichever of S(next) and P.V(next) is ready first.
     if (lane == 0) {
       bool ok = mbar_wait_bounded(&bar[B_Q], 0, p.status);
       int ns = 0, npv = 0;  // next S tile, next P.V tile
-      uint64_t since = global_ns();
+      // The timeout clock (%globaltimer) is read only every 256 idle polls and
+      // restarts whenever an MMA is issued.
+      uint32_t idle = 0;
+      uint64_t idle_since = 0;
       while (ok && npv < my_n) {
         bool progress = false;
         if (ns < my_n) {
@@ -336,15 +303,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         if (progress) {
-          since = global_ns();
-        } else {
-          if (*(volatile int *)abort_flag) {
-            ok = false;
-          } else if (global_ns() - since > kWaitLimitNs) {
+          idle = 0;
+          idle_since = 0;
+        } else if (*(volatile int *)abort_flag) {
+          ok = false;
+        } else if ((++idle & 255u) == 0) {
+          const uint64_t now = global_ns();
+          if (idle_since == 0) {
+            idle_since = now;
+          } else if (now - idle_since > kWaitLimitNs) {
             flag_status(p.status, MI_DEV_TIMEOUT);
             ok = false;
-          } else {
-            __nanosleep(32);
           }
         }
       }
@@ -358,6 +327,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q4 = warp & 3;
     const int k = q4 * 32 + lane;  // key of the tile (S^T lane) / dimension (O^T lane)
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    // This step's token: dimension k of its K and V rows (produced by the
+    // preceding kernel, so read after the dependency wait).
+    float kn = 0.f, vn = 0.f;
+    if (own_new) {
+      if (p.early_kv) pdl_wait();
+      const int64_t off = seq * p.new_token_stride_bytes + static_cast<int64_t>(kvh) * 256 + k * 2;
+      kn = Elem<T>::to_float(*reinterpret_cast<const T *>(p.k_new + off));
+      vn = Elem<T>::to_float(*reinterpret_cast<const T *>(p.v_new + off));
+    }
     float m[G], lp[G];
 #pragma unroll
     for (int h = 0; h < G; ++h) {
@@ -380,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       mbar_arrive(&bar[B_SEMPTY + b]);
 
-      const bool valid = tile_of(it) * 128 + k < ctx;
+      const bool valid = tile_of(it) * 128 + k < ctx_kv;
       float x[G];
 #pragma unroll
       for (int h = 0; h < G; ++h) x[h] = valid ? sv[h] * p.scale_log2 : -INFINITY;
@@ -473,31 +451,56 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float s = warp_sum(lp[h]);
       if (lane == 0) lred[q4 * 8 + h] = s;
     }
-    softmax_sync_any(false);
+    float snew[G];
+    if (own_new) {
+      // q_h . k_new over the 128 dimensions (thread k holds dimension k)
+      if (my_n == 0) mbar_wait_bounded(&bar[B_Q], 0, p.status);
+      float *dred = red + 96;
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const uint32_t qaddr = sQ + (k >> 6) * 2048 + h * 128 + ((((k & 63) >> 3) ^ (h & 7)) << 4) +
+                               (k & 7) * 2;
+        unsigned short raw;
+        asm volatile("ld.shared.b16 %0, [%1];" : "=h"(raw) : "r"(qaddr) : "memory");
+        const float part = warp_sum(Elem<T>::to_float(*reinterpret_cast<const T *>(&raw)) * kn);
+        if (lane == 0) dred[q4 * 8 + h] = part;
+      }
+      softmax_sync_any(false);
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+        snew[h] = (dred[h] + dred[8 + h] + dred[16 + h] + dred[24 + h]) * p.scale_log2;
+    } else {
+      softmax_sync_any(false);
+    }
     const int d = k;
-    float *fin_acc = reinterpret_cast<float *>(smem + kOffK);  // aliases the drained K ring
-    float *fin_ml = fin_acc + 8 * 128;
 #pragma unroll
     for (int h = 0; h < G; ++h) {
-      const float L = lred[h] + lred[8 + h] + lred[16 + h] + lred[24 + h];
-      const float M = m[h];
+      float L = lred[h] + lred[8 + h] + lred[16 + h] + lred[24 + h];
+      float M = m[h];
+      float A = o[h];
+      if (own_new) {
+        const float mn = fmaxf(M, snew[h]);
+        const float alpha = M == -INFINITY ? 0.f : fast_exp2(M - mn);
+        const float pn = fast_exp2(snew[h] - mn);
+        A = A * alpha + pn * vn;
+        L = L * alpha + pn;
+        M = mn;
+      }
       const int qh = kvh * G + h;
       if (nsplit == 1) {
         T *orow = static_cast<T *>(p.out) + (seq * p.num_q_heads + qh) * 128;
-        orow[d] = Elem<T>::from_float(L > 0.f ? o[h] / L : 0.f);
-      } else if (p.cluster_combine) {
-        fin_acc[h * 128 + d] = o[h];
-        if (d == 0) {
-          fin_ml[h * 2] = M;
-          fin_ml[h * 2 + 1] = L;
-        }
+        orow[d] = Elem<T>::from_float(L > 0.f ? A / L : 0.f);
       } else {
-        const int64_t state = (seq * p.num_q_heads + qh) * nsplit + split;
-        p.ws_acc[state * 128 + d] = o[h];
-        if (d == 0) {
-          p.ws_ml[state * 2] = M;
-          p.ws_ml[state * 2 + 1] = L;
-        }
+        split_store_state(p, seq, qh, nsplit, split, 128, d, M, L, A);
+      }
+    }
+    if (own_new) {
+      if (slot < p.num_blocks * p.block_size) {
+        const int64_t off = (slot * p.num_kv_heads + kvh) * 256 + k * 2;
+        *reinterpret_cast<T *>(const_cast<char *>(p.key_cache) + off) = Elem<T>::from_float(kn);
+        *reinterpret_cast<T *>(const_cast<char *>(p.value_cache) + off) = Elem<T>::from_float(vn);
+      } else if (k == 0) {
+        flag_status(p.status, MI_DEV_BAD_SLOT);
       }
     }
   }
@@ -505,45 +508,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_launch_dependents();
   tc::fence_before_sync();
   __syncthreads();
-  if (p.cluster_combine && nsplit > 1) {
-    cg::cluster_group cluster = cg::this_cluster();
-    float *fin_acc = reinterpret_cast<float *>(smem + kOffK);
-    float *fin_ml = fin_acc + 8 * 128;
-    cluster.sync();
-    for (int i = split * kThreads + threadIdx.x; i < G * 128; i += nsplit * kThreads) {
-      const int h = i / 128, d = i % 128;
-      float ms[8], ls[8], as[8];
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        if (s < nsplit) {
-          const float *rml = cluster.map_shared_rank(fin_ml, s);
-          ms[s] = rml[h * 2];
-          ls[s] = rml[h * 2 + 1];
-          as[s] = cluster.map_shared_rank(fin_acc, s)[h * 128 + d];
-        }
-      }
-      float M = -INFINITY;
-#pragma unroll
-      for (int s = 0; s < 8; ++s)
-        if (s < nsplit) M = fmaxf(M, ms[s]);
-      float L = 0.f, A = 0.f;
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        if (s < nsplit) {
-          const float f = ms[s] == -INFINITY ? 0.f : fast_exp2(ms[s] - M);
-          L += f * ls[s];
-          A += f * as[s];
-        }
-      }
-      T *orow = static_cast<T *>(p.out) + (seq * p.num_q_heads + kvh * G + h) * 128;
-      orow[d] = Elem<T>::from_float(L > 0.f ? A / L : 0.f);
-    }
-    cluster.sync();
-  }
   if (warp == 1) {
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, kTmemCols);
   }
+  if (nsplit > 1) split_arrive_and_merge<T, G, 128>(p, seq, kvh, nsplit, abort_flag + 1);
 }
 
 namespace {
@@ -591,15 +560,8 @@ cudaError_t launch_tg(const DecodeTcParams &P, int64_t num_seqs, int nsplit, cud
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[1];
   int n = 0;
-  if (P.d.cluster_combine && nsplit > 1) {
-    attr[n].id = cudaLaunchAttributeClusterDimension;
-    attr[n].val.clusterDim.x = nsplit;
-    attr[n].val.clusterDim.y = 1;
-    attr[n].val.clusterDim.z = 1;
-    ++n;
-  }
   if (pdl_enabled()) {
     attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[n].val.programmaticStreamSerializationAllowed = 1;
@@ -611,9 +573,6 @@ cudaError_t launch_tg(const DecodeTcParams &P, int64_t num_seqs, int nsplit, cud
 }
 
 }  // namespace
-
-cudaError_t launch_decode_combine(const DecodeParams &p, int dtype, int D, int64_t num_seqs,
-                                  int nsplit, cudaStream_t stream);
 
 bool decode_tc_supported(int dtype, int D, int G, int block_size) {
   if (dtype != MI_DTYPE_BFLOAT16 && dtype != MI_DTYPE_FLOAT16) return false;
@@ -656,8 +615,7 @@ cudaError_t launch_decode_tc(const DecodeParams &d, int dtype, int G, int64_t nu
       default: e = launch_tg<__half, 8>(P, num_seqs, nsplit, stream); break;
     }
   }
-  if (e != cudaSuccess || nsplit == 1 || d.cluster_combine) return e;
-  return launch_decode_combine(d, dtype, 128, num_seqs, nsplit, stream);
+  return e;
 }
 
 }  // namespace mi

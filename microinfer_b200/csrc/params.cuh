@@ -74,8 +74,10 @@ struct DecodeParams {
   const char *value_cache;
   const int32_t *block_tables;
   const int32_t *context_lens;
+  // Split-K workspace (nsplit > 1): states and self-resetting arrival counters.
   float *ws_acc;
   float *ws_ml;
+  int32_t *ws_count;
   int64_t bt_stride;
   int64_t num_blocks;
   int32_t block_size;
@@ -88,9 +90,6 @@ struct DecodeParams {
   const char *v_new;
   const int32_t *slot_mapping;  // int32 [num_seqs]; -1 = padding row, no store
   int64_t new_token_stride_bytes;
-  // 1: the splits of one (seq, kv head) form a thread-block cluster and are
-  // merged through distributed shared memory (no workspace, no combine launch).
-  int32_t cluster_combine;
   // 1: read the block table, context lengths and cached pages before waiting
   // on the preceding kernel (programmatic dependent launch), so this layer's
   // page loads overlap the previous kernel's tail.  Only q and this step's

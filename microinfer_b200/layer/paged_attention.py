@@ -10,8 +10,11 @@ dispatch targets:
 
 Unlike the reference there is one kernel family for every block size and
 no FlashAttention, Triton or torch fallback: CPU tensors and shapes no kernel
-takes raise.  Workspace for split-K decode is allocated per call from the
-caching allocator (the graph pool during capture), like the reference.
+takes raise.  Split-K decode merges its splits in the kernel (the last split
+to finish merges) through one zero-filled workspace per device that the
+kernels leave zeroed, so it is allocated once and reused by every launch,
+CUDA graph replays included; launches on one device are expected to run one
+at a time, as in the reference's single-stream engine.
 """
 
 from __future__ import annotations
@@ -29,6 +32,23 @@ def _idx(t: torch.Tensor) -> torch.Tensor:
     if t.dtype != torch.int32:
         t = t.to(torch.int32)
     return t.contiguous()
+
+
+_WORKSPACES: dict[int, list[torch.Tensor]] = {}
+
+
+def _split_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """The device's split-K workspace, at least ``nbytes`` long and zero-filled.
+
+    The decode kernels restore its arrival counters to zero, so it is zeroed
+    only when allocated.  Outgrown buffers stay alive: a captured CUDA graph
+    keeps their addresses.
+    """
+    bufs = _WORKSPACES.setdefault(device.index or 0, [])
+    if not bufs or bufs[-1].numel() * 4 < nbytes:
+        size = max(nbytes, 1 << 20)
+        bufs.append(torch.zeros((size + 3) // 4, dtype=torch.float32, device=device))
+    return bufs[-1]
 
 
 def _check_common(query, key_cache, value_cache):
@@ -107,9 +127,7 @@ def _decode_prep(query, key_cache, value_cache, block_tables, context_lens, spli
     _, split_k, ws_bytes = decode_plan(num_requests, num_q_heads, num_kv_heads, head_dim,
                                        query.dtype, block_size, split_k, device,
                                        block_tables.shape[1])
-    workspace = None
-    if ws_bytes:
-        workspace = torch.empty(ws_bytes // 4, dtype=torch.float32, device=device)
+    workspace = _split_workspace(device, ws_bytes) if ws_bytes else None
     return dict(
         query=query.contiguous(), block_tables=_idx(block_tables), context_lens=_idx(context_lens),
         out=torch.empty_like(query) if out is None else out, device=device, split_k=split_k,

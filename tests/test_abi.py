@@ -47,13 +47,19 @@ def test_abi_version():
 def test_workspace_and_split_policy():
     lib = _lib.load()
     assert lib.mi_paged_decode_workspace_bytes(8, 16, 128, 1) == 0
-    assert lib.mi_paged_decode_workspace_bytes(8, 16, 128, 5) == 8 * 16 * 5 * 130 * 4
-    # 148 SMs assumed without a device: floor(2*148 / (8*8)) = 4 (one wave)
-    assert lib.mi_paged_decode_default_splits(8, 8, 0, 0) == 4
+    # a fixed 64 KiB region of arrival counters, then the split states
+    assert lib.mi_paged_decode_workspace_bytes(8, 16, 128, 5) == 65536 + 8 * 16 * 5 * 130 * 4
+    assert lib.mi_paged_decode_workspace_bytes(1, 4, 64, 2) == 65536 + 1 * 4 * 2 * 66 * 4
+    # 148 SMs assumed without a device.  Small batches stay within half the
+    # SMs (74 CTAs) so the next layer's CTAs fit beside them: 74 // (8*8) = 1
+    assert lib.mi_paged_decode_default_splits(8, 8, 0, 0) == 1
+    assert lib.mi_paged_decode_default_splits(1, 8, 0, 0) == 9
+    # ... and a context hint gives each split >= 384 keys
+    assert lib.mi_paged_decode_default_splits(1, 8, 256, 0) == 1
+    assert lib.mi_paged_decode_default_splits(1, 8, 2000, 0) == 6
+    # larger batches: one wave of two CTAs per SM, >= 2 chunks of 8 keys per warp
+    assert lib.mi_paged_decode_default_splits(16, 8, 0, 0) == 2
     assert lib.mi_paged_decode_default_splits(256, 8, 0, 0) == 1
-    assert lib.mi_paged_decode_default_splits(1, 8, 0, 0) == 37
-    # a context hint caps splits at >= 2 chunks per warp
-    assert lib.mi_paged_decode_default_splits(1, 8, 256, 0) == 2
 
 
 def _decode_args(**over):
@@ -84,9 +90,9 @@ def test_decode_rejects_invalid_arguments_before_launch(over, fragment):
         _lib.check(status)
 
 
-def test_workspace_needed_only_beyond_cluster_merge():
+def test_workspace_needed_for_every_split_count_above_one():
     lib = _lib.load()
-    assert [lib.mi_paged_decode_uses_workspace(s) for s in (1, 2, 8, 9, 37)] == [0, 0, 0, 1, 1]
+    assert [lib.mi_paged_decode_uses_workspace(s) for s in (1, 2, 8, 9, 37)] == [0, 1, 1, 1, 1]
 
 
 def test_decode_with_no_sequences_is_a_no_op():

@@ -7,6 +7,7 @@ gather and copy-on-write; attention within 2e-2 abs / 1e-2 rel for fp16/bf16
 """
 
 import math
+import os
 
 import numpy as np
 import pytest
@@ -159,6 +160,58 @@ def test_fused_store_skips_padding_slots():
     np.testing.assert_array_equal(host(kc, dt)[s0 // 16, s0 % 16], before[s0 // 16, s0 % 16])
     s1 = int(case["slots"][1])
     np.testing.assert_array_equal(host(kc, dt)[s1 // 16, s1 % 16], case["k_new"][1])
+
+
+@pytest.mark.parametrize("width", [4, 160])  # table bound 64 keys (SIMT) / 2560 keys (tcgen05)
+@pytest.mark.parametrize("split_k,early_kv", [(1, False), (3, True)])
+def test_fused_store_with_only_the_new_token(width, split_k, early_kv):
+    """Context 1: the token being stored is the whole context, so out = v_new."""
+    n, hq, hkv, d, bs = 3, 16, 8, 128, 16
+    kernel, _, _ = mi.decode_plan(n, hq, hkv, d, torch.bfloat16, bs, split_k, "cuda", width)
+    if "MICROINFER_B200_DECODE" not in os.environ:  # not pinned to one kernel
+        assert kernel == ("tcgen05" if width * bs >= 2048 else "simt")
+    g = torch.Generator(device="cuda").manual_seed(3)
+    kc = torch.randn(8, bs, hkv, d, generator=g, device="cuda").to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    q = torch.randn(n, hq, d, generator=g, device="cuda").to(torch.bfloat16)
+    kn = torch.randn(n, hkv, d, generator=g, device="cuda").to(torch.bfloat16)
+    vn = torch.randn(n, hkv, d, generator=g, device="cuda").to(torch.bfloat16)
+    table = torch.full((n, width), -1, dtype=torch.int32, device="cuda")
+    table[:, 0] = torch.tensor([5, 2, 7], dtype=torch.int32)
+    ctx = torch.ones(n, dtype=torch.int32, device="cuda")
+    slots = (table[:, 0] * bs).to(torch.int32)
+    out = mi.paged_decode_store(q, kc, vc, table, ctx, kn, vn, slots, split_k=split_k,
+                                early_kv=early_kv)
+    torch.cuda.synchronize()
+    expected = vn.repeat_interleave(hq // hkv, dim=1)
+    torch.testing.assert_close(out, expected, atol=0, rtol=0)
+    torch.testing.assert_close(kc[table[:, 0].long(), 0], kn, atol=0, rtol=0)
+    torch.testing.assert_close(vc[table[:, 0].long(), 0], vn, atol=0, rtol=0)
+
+
+@pytest.mark.parametrize("width", [40, 160])  # SIMT / tcgen05 kernel
+def test_split_workspace_counters_return_to_zero(width):
+    """The last split to finish resets its arrival counter, so the shared
+    workspace serves the next launch of any shape (fresh inputs every launch,
+    so a skipped merge cannot pass on a stale output)."""
+    from microinfer_b200.layer import paged_attention as pa
+
+    g = torch.Generator(device="cuda").manual_seed(9)
+    kc = (torch.randn(640, 16, 8, 128, generator=g, device="cuda") * 0.5).to(torch.bfloat16)
+    vc = (torch.randn_like(kc, dtype=torch.float32) * 0.5).to(torch.bfloat16)
+    for n, hq in ((1, 32), (64, 16), (3, 8), (16, 64)):
+        table = torch.full((n, width), -1, dtype=torch.int32, device="cuda")
+        table[:, :32] = torch.randint(0, 640, (n, 32), generator=g, device="cuda",
+                                      dtype=torch.int32)
+        ctx = torch.randint(1, 513, (n,), generator=g, device="cuda", dtype=torch.int32)
+        for split in (2, 5, 37):
+            q = torch.randn(n, hq, 128, generator=g, device="cuda").to(torch.bfloat16)
+            ref = mi.paged_decode(q, kc, vc, table, ctx, split_k=1)
+            out = mi.paged_decode(q, kc, vc, table, ctx, split_k=split)
+            torch.testing.assert_close(out, ref, atol=2e-2, rtol=1e-2)
+    torch.cuda.synchronize()
+    for ws in pa._WORKSPACES[torch.cuda.current_device()]:
+        assert int(ws.view(torch.int32)[:16384].abs().sum().item()) == 0
 
 
 @pytest.mark.parametrize("name", ["cfg1_decode_f32", "cfg2_layer_bf16", "decode_bs64_bf16"])

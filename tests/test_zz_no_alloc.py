@@ -43,7 +43,8 @@ def _with_workspace(q, kc, vc, table, ctx, splits, status, stream):
     n, hq, d = q.shape
     out = torch.empty_like(q)
     ws_bytes = lib.mi_paged_decode_workspace_bytes(n, hq, d, splits)
-    ws = torch.empty(max(ws_bytes // 4, 1), dtype=torch.float32, device=q.device)
+    # zero-filled once: the kernels leave the split-K arrival counters at zero
+    ws = torch.zeros(max(ws_bytes // 4, 1), dtype=torch.float32, device=q.device)
     _lib.check(lib.mi_paged_decode(
         out.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), kc.shape[0], kc.shape[1],
         hq, kc.shape[2], d, 2, table.data_ptr(), table.stride(0), ctx.data_ptr(), n,
