@@ -29,8 +29,21 @@
 #include "launch.cuh"
 #include "params.cuh"
 #include "split_merge.cuh"
+#include "tc_helpers.cuh"
+#include "tmap.cuh"
 
 namespace mi {
+
+// Launch parameters: the decode arguments plus, when every 8-key chunk lies
+// in one page (block_size % 8 == 0) and a row is at most 256 bytes, tensor
+// maps over the K and V pools ([slots][Hkv][D], box {D, 1, 8}, no swizzle)
+// so that a chunk's rows of one head arrive in one TMA copy each.
+struct __align__(64) DecodeSimtParams {
+  CUtensorMap tmap_k;
+  CUtensorMap tmap_v;
+  DecodeParams d;
+  int32_t use_tma;
+};
 
 namespace {
 constexpr unsigned kFull = 0xffffffffu;
@@ -98,8 +111,11 @@ __device__ __forceinline__ void transpose_reduce(float (&v)[N], int c) {
 }
 
 template <typename T, int D, int G, int W>
-__global__ void __launch_bounds__(W * 32, (W == 8 && G < 8) ? 2 : 1) paged_decode_kernel(DecodeParams p) {
+__global__ void __launch_bounds__(W * 32, (W == 8 && G < 8) ? 2 : 1)
+    paged_decode_kernel(const __grid_constant__ DecodeSimtParams P) {
   using C = DecCfg<T, D, G, W>;
+  const DecodeParams &p = P.d;
+  const bool use_tma = P.use_tma != 0;
   extern __shared__ __align__(128) char smem[];
   char *stage_mem = smem;
   float *p_smem = reinterpret_cast<float *>(smem + C::kSmemStages);
@@ -136,9 +152,12 @@ __global__ void __launch_bounds__(W * 32, (W == 8 && G < 8) ? 2 : 1) paged_decod
     const int64_t col = (static_cast<int64_t>(ci) * C::kKeys + copy_key) / p.block_size;
     return col < p.bt_stride ? static_cast<int64_t>(__ldg(table + col)) : -1;
   };
-  int64_t pre_blk[C::kStages];
+  // Block-table window: win[j] is this lane's entry for chunk it + j of the
+  // warp's loop (entries are loaded kWin - kStages iterations before use).
+  constexpr int kWin = C::kStages + kL2Ahead;
+  int32_t win[kWin];  // block ids are int32 in the table
 #pragma unroll
-  for (int s = 0; s < C::kStages; ++s) pre_blk[s] = table_entry(chunk_of(s));
+  for (int j = 0; j < kWin; ++j) win[j] = static_cast<int32_t>(table_entry(chunk_of(j)));
   int ctx = __ldg(p.context_lens + seq);
   const int64_t slot = fused ? static_cast<int64_t>(__ldg(p.slot_mapping + seq)) : -1;
 
@@ -172,6 +191,20 @@ __global__ void __launch_bounds__(W * 32, (W == 8 && G < 8) ? 2 : 1) paged_decod
     return blk;
   };
   auto issue = [&](int ci, int st, int64_t blk) {
+    if (use_tma) {  // one 8-row copy each for K and V (lane 0's entry is the chunk's page)
+      if (lane == 0) {
+        if (blk >= 0) {
+          const int row = static_cast<int>(blk * p.block_size + (ci * C::kKeys) % p.block_size);
+          char *dst = wstage + st * C::kStageBytes;
+          mbar_arrive_expect_tx(&wbar[st], 2 * C::kKeys * C::kRowBytes);
+          tc::tma_load_3d(dst, &P.tmap_k, 0, kvh, row, &wbar[st]);
+          tc::tma_load_3d(dst + C::kKeys * C::kRowBytes, &P.tmap_v, 0, kvh, row, &wbar[st]);
+        } else {
+          mbar_arrive(&wbar[st]);
+        }
+      }
+      return;
+    }
     const int key = ci * C::kKeys + copy_key;
     const bool go = blk >= 0;
     const unsigned mask = __ballot_sync(kFull, go);
@@ -191,21 +224,29 @@ __global__ void __launch_bounds__(W * 32, (W == 8 && G < 8) ? 2 : 1) paged_decod
   for (int s = 0; s < C::kStages; ++s) {
     if (s < my_n) {
       const int ci = chunk_of(s);
-      issue(ci, s, check_blk(ci, pre_blk[s]));
+      issue(ci, s, check_blk(ci, win[s]));
       ++issued;
     }
   }
   // Chunks beyond the ring: warm L2 with their rows now, so their copies come
   // from L2 once the ring drains (bad ids are only skipped here; the copy
   // itself flags them).
-#pragma unroll 1
-  for (int it = C::kStages; it < my_n && it < C::kStages + kL2Ahead; ++it) {
-    const int ci = chunk_of(it);
+#pragma unroll
+  for (int j = C::kStages; j < kWin; ++j) {
+    const int ci = chunk_of(j);
     const int key = ci * C::kKeys + copy_key;
-    const int64_t blk = table_entry(ci);
-    if (copy_lane && key < ctx_kv && blk >= 0 && blk < p.num_blocks)
+    const int64_t blk = win[j];
+    if (j >= my_n || blk < 0 || blk >= p.num_blocks) continue;
+    if (use_tma) {
+      if (lane == 0) {
+        const int row = static_cast<int>(blk * p.block_size + (ci * C::kKeys) % p.block_size);
+        tc::tma_prefetch_l2_3d(&P.tmap_k, 0, kvh, row);
+        tc::tma_prefetch_l2_3d(&P.tmap_v, 0, kvh, row);
+      }
+    } else if (copy_lane && key < ctx_kv) {
       prefetch_l2_bulk(kv_src_base + (blk * p.block_size + key % p.block_size) * tok_bytes,
                        C::kRowBytes);
+    }
   }
   if (p.early_kv) {
     pdl_launch_dependents();  // the next kernel may start its own prologue
@@ -278,7 +319,6 @@ __global__ void __launch_bounds__(W * 32, (W == 8 && G < 8) ? 2 : 1) paged_decod
     const int ci = chunk_of(it);
     const bool has_next = it + C::kStages < my_n;
     const int nci = chunk_of(it + C::kStages);
-    const int64_t nblk_raw = has_next ? table_entry(nci) : -1;
     if (!mbar_wait_bounded(&wbar[st], parity, p.status)) {
       timed_out = true;
       break;
@@ -397,9 +437,14 @@ __global__ void __launch_bounds__(W * 32, (W == 8 && G < 8) ? 2 : 1) paged_decod
     // FMAs above), so the stage can be refilled: no proxy fence needed.
     __syncwarp();
     if (has_next) {
-      issue(nci, st, check_blk(nci, nblk_raw));
+      issue(nci, st, check_blk(nci, win[C::kStages]));
       ++issued;
     }
+    // Slide the window one chunk on; the new entry is first used kL2Ahead
+    // iterations from now.
+#pragma unroll
+    for (int j = 0; j < kWin - 1; ++j) win[j] = win[j + 1];
+    win[kWin - 1] = it + kWin < my_n ? static_cast<int32_t>(table_entry(chunk_of(it + kWin))) : -1;
   }
   if (timed_out) {
     // Let every copy still in flight land before the stage memory is reused.
@@ -533,11 +578,31 @@ __global__ void __launch_bounds__(W * 32, (W == 8 && G < 8) ? 2 : 1) paged_decod
   if (nsplit > 1) split_arrive_and_merge<T, G, D>(p, seq, kvh, nsplit, last_flag);
 }
 
+template <typename T>
+constexpr CUtensorMapDataType tmap_dtype() {
+  return Elem<T>::kDtype == MI_DTYPE_FLOAT32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+         : Elem<T>::kDtype == MI_DTYPE_FLOAT16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                               : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+}
+
 template <typename T, int D, int G, int W>
 static cudaError_t launch_decode_tdgw(const DecodeParams &p, int64_t num_seqs, int nsplit,
                                       cudaStream_t stream) {
   using C = DecCfg<T, D, G, W>;
   auto kern = paged_decode_kernel<T, D, G, W>;
+  DecodeSimtParams P;
+  memset(&P, 0, sizeof(P));
+  P.d = p;
+  const uint64_t rows = static_cast<uint64_t>(p.num_blocks) * p.block_size;
+  if (C::kRowBytes <= 256 && p.block_size % C::kKeys == 0 && rows < (1ull << 31)) {
+    const uint64_t row_stride = static_cast<uint64_t>(p.num_kv_heads) * C::kRowBytes;
+    P.use_tma = encode_rows_map(&P.tmap_k, tmap_dtype<T>(), p.key_cache, D, p.num_kv_heads, rows,
+                                C::kRowBytes, row_stride, D, 1, C::kKeys,
+                                CU_TENSOR_MAP_SWIZZLE_NONE) &&
+                encode_rows_map(&P.tmap_v, tmap_dtype<T>(), p.value_cache, D, p.num_kv_heads,
+                                rows, C::kRowBytes, row_stride, D, 1, C::kKeys,
+                                CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -547,7 +612,7 @@ static cudaError_t launch_decode_tdgw(const DecodeParams &p, int64_t num_seqs, i
     attr_set[dev] = true;
   }
   const dim3 grid(nsplit, p.num_kv_heads, static_cast<unsigned>(num_seqs));
-  return launch_pdl(kern, grid, dim3(C::kThreads), C::kSmem, stream, p);
+  return launch_pdl(kern, grid, dim3(C::kThreads), C::kSmem, stream, P);
 }
 
 template <typename T, int D, int G>

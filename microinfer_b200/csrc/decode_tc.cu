@@ -39,6 +39,7 @@
 #include "params.cuh"
 #include "split_merge.cuh"
 #include "tc_helpers.cuh"
+#include "tmap.cuh"
 
 namespace mi {
 
@@ -517,31 +518,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 namespace {
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn_dec() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
 bool encode(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t heads,
             uint64_t rows, uint64_t row_stride_bytes, uint32_t box_y, uint32_t box_z) {
-  auto fn = encode_fn_dec();
-  if (fn == nullptr) return false;
-  cuuint64_t dims[3] = {128, heads, rows};
-  cuuint64_t strides[2] = {256, row_stride_bytes};
-  cuuint32_t box[3] = {64, box_y, box_z};
-  cuuint32_t estr[3] = {1, 1, 1};
-  return fn(map, dt, 3, const_cast<void *>(base), dims, strides, box, estr,
-            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return encode_rows_map(map, dt, base, 128, heads, rows, 256, row_stride_bytes, 64, box_y, box_z,
+                         CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 template <typename T, int G>
@@ -578,7 +558,7 @@ bool decode_tc_supported(int dtype, int D, int G, int block_size) {
   if (dtype != MI_DTYPE_BFLOAT16 && dtype != MI_DTYPE_FLOAT16) return false;
   if (D != 128 || (G != 1 && G != 2 && G != 4 && G != 8)) return false;
   if (block_size < 16 || block_size % 16 != 0) return false;
-  return encode_fn_dec() != nullptr;
+  return tensor_map_encoder() != nullptr;
 }
 
 cudaError_t launch_decode_tc(const DecodeParams &d, int dtype, int G, int64_t num_seqs,
