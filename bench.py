@@ -37,6 +37,14 @@ METRIC = "paged decode attn HBM GB/s (Qwen3-0.6B decode step, store+decode x28 l
 WORKLOAD = "BASELINE configs[1]: Qwen3-0.6B decode step, bf16, 28 layers, batch 8/GPU"
 
 
+# kernel names for the roofline entry and the ncu summaries that measured them
+DECODE_KERNEL_NAMES = {"mma": "paged_decode_mma_kernel", "simt": "paged_decode_kernel",
+                       "tcgen05": "paged_decode_tc_kernel", "generic": "attn_generic_kernel"}
+DECODE_PROFILES = {"mma": "decode_mma_qwen3_0.6b_config2.md",
+                   "simt": "decode_simt_qwen3_0.6b_config2.md",
+                   "tcgen05": "decode_tc_qwen3_8b_32k.md"}
+
+
 def _peaks():
     try:
         return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
@@ -556,17 +564,15 @@ def run_ours(args):
             "tok_per_s": round(world * NSEQ / (ms_step * 1e-3), 1),
             "median_step_ms": round(statistics.median(per_step), 5),
             "roofline": {"bound": "hbm",
-                         "kernel": ("paged_decode_tc_kernel" if decode_kernel == "tcgen05"
-                                    else "paged_decode_kernel") + " (store fused, split merge)",
+                         "kernel": DECODE_KERNEL_NAMES.get(decode_kernel, decode_kernel)
+                                   + " (store fused, split merge)",
                          "achieved": round(achieved, 1),
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": round(achieved / peaks["hbm_gbs"], 4),
                          "peak_source": f"hbm_gbs of {peak_src}",
                          "avg_launch_us": round(decode_launch_ms * 1e3, 3),
                          "algorithmic_bytes_per_launch": dec_b + st_b,
-                         "traffic": _profiled_traffic(
-                             "decode_tc_qwen3_8b_32k.md" if decode_kernel == "tcgen05"
-                             else "decode_simt_qwen3_0.6b_config2.md"),
+                         "traffic": _profiled_traffic(DECODE_PROFILES.get(decode_kernel, "")),
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
                                            "profiles/ summary of the same kernel and shapes",
                          "step_frac": round(value / world / peaks["hbm_gbs"], 4)},

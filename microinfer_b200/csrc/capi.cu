@@ -23,6 +23,9 @@ cudaError_t launch_wait_flag(const int32_t *flag, int64_t timeout_ns, int32_t *s
 cudaError_t launch_attn_generic(const AttnParams &p, int dtype, bool paged, cudaStream_t stream);
 bool decode_fast_supported(int dtype, int D, int G);
 bool decode_tc_supported(int dtype, int D, int G, int block_size);
+bool decode_mma_supported(int dtype, int D, int G, int block_size);
+cudaError_t launch_decode_mma(const DecodeParams &d, int dtype, int D, int G, int64_t num_seqs,
+                              int nsplit, cudaStream_t stream);
 cudaError_t launch_decode_tc(const DecodeParams &d, int dtype, int G, int64_t num_seqs,
                              int64_t num_blocks, int nsplit, cudaStream_t stream);
 cudaError_t launch_decode_fast(const DecodeParams &p, int dtype, int D, int G, int64_t num_seqs,
@@ -219,9 +222,12 @@ int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads, int32
     // take that room away.  Each split gets at least kDecodeKeysPerCta keys.
     s = (sms / 2) / base;
     if (max_context_hint > 0) {
-      const int64_t cap = (static_cast<int64_t>(max_context_hint) + kDecodeKeysPerCta - 1) /
-                          kDecodeKeysPerCta;
-      if (s > cap) s = cap;
+      const int64_t need = (static_cast<int64_t>(max_context_hint) + kDecodeKeysPerCta - 1) /
+                           kDecodeKeysPerCta;
+      if (need > 2 * s)
+        s = sms / base;  // long contexts stream for longer than a launch: use every SM
+      else if (s > need)
+        s = need;
     }
   } else {
     // Larger batch: one wave of two CTAs per SM.
@@ -252,27 +258,26 @@ namespace {
 // Split-K merges through the workspace (last-arriver, split_merge.cuh).
 bool decode_uses_workspace(int nsplit) { return nsplit > 1; }
 
-// Decode kernels, in order of preference: tcgen05 (tensor-core, D=128 fp16 /
-// bf16, block size a multiple of 16), SIMT (bulk-copy staged, CUDA cores),
-// generic (any shape).  MICROINFER_B200_DECODE=simt|tc pins one.
-constexpr int kDecodeGeneric = 1, kDecodeSimt = 2, kDecodeTc = 3;
-
-// Contexts of at least this many keys (bounded by the block-table width)
-// stream long enough for the tensor-core kernel to win; shorter ones are
-// latency-bound and run on the SIMT kernel, which is quicker to start.
-constexpr int64_t kTcMinContext = 2048;
+// Decode kernels, in order of preference: warp-level tensor-core MMA
+// (mma.sync, bf16/fp16, D 64/128, block size a multiple of 16), SIMT
+// (TMA-staged, CUDA cores, every fast shape), generic (any shape).  The
+// tcgen05 swap-AB kernel (D=128) is kept behind MICROINFER_B200_DECODE=tc;
+// =simt and =mma pin those kernels.
+constexpr int kDecodeGeneric = 1, kDecodeSimt = 2, kDecodeTc = 3, kDecodeMma = 4;
 
 int decode_kernel_for(int dtype, int D, int G, int block_size, bool aligned, int64_t max_context) {
+  (void)max_context;
   static const int mode = [] {
     const char *v = std::getenv("MICROINFER_B200_DECODE");
     if (v != nullptr && std::strcmp(v, "simt") == 0) return 1;
     if (v != nullptr && std::strcmp(v, "tc") == 0) return 2;
+    if (v != nullptr && std::strcmp(v, "mma") == 0) return 3;
     return 0;
   }();
   if (!aligned || !decode_fast_supported(dtype, D, G)) return kDecodeGeneric;
-  const bool tc_ok = decode_tc_supported(dtype, D, G, block_size);
-  if (mode == 2 && tc_ok) return kDecodeTc;
-  if (mode == 0 && tc_ok && max_context >= kTcMinContext) return kDecodeTc;
+  if (mode == 2 && decode_tc_supported(dtype, D, G, block_size)) return kDecodeTc;
+  if (mode == 1) return kDecodeSimt;
+  if (decode_mma_supported(dtype, D, G, block_size)) return kDecodeMma;
   return kDecodeSimt;
 }
 
@@ -282,7 +287,7 @@ int decode_splits_for(int kernel, int64_t num_seqs, int num_kv_heads, int num_sp
                       int64_t ctx_bound) {
   if (num_splits > 0) return num_splits;
   if (kernel == kDecodeGeneric) return 1;
-  if (kernel == kDecodeSimt) {
+  if (kernel == kDecodeSimt || kernel == kDecodeMma) {
     const int64_t hint = ctx_bound > INT32_MAX ? INT32_MAX : ctx_bound;
     return mi_paged_decode_default_splits(num_seqs, num_kv_heads, static_cast<int32_t>(hint), dev);
   }
@@ -420,6 +425,10 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
   if (kernel == kDecodeTc) {
     const cudaError_t te = launch_decode_tc(p, dtype, G, num_seqs, num_blocks, nsplit, st);
     if (te != cudaErrorNotSupported) return cuda_status(te);
+  }
+  if (kernel == kDecodeMma) {
+    const cudaError_t me = launch_decode_mma(p, dtype, head_dim, G, num_seqs, nsplit, st);
+    if (me != cudaErrorNotSupported) return cuda_status(me);
   }
   return cuda_status(launch_decode_fast(p, dtype, head_dim, G, num_seqs, nsplit,
                                         decode_simt_wide(dtype, head_dim, G, num_seqs * num_kv_heads * nsplit, dev),
