@@ -358,6 +358,19 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
       issue(chunk_of(it + kStagesM), st, checked(win[kStagesM]));
       ++issued;
     }
+    // Rolling L2 prefetch of the chunk kWin - 1 ahead (the prologue covered
+    // the first kWin), so long contexts keep kWin chunks per warp in flight.
+    if (it > 0 && lane == 0 && it + kWin - 1 < my_n) {
+      const int32_t blk = win[kWin - 1];
+      if (blk >= 0 && blk < p.num_blocks) {
+        const int row = row_of(chunk_of(it + kWin - 1), blk);
+#pragma unroll
+        for (int h = 0; h < C::kHalves; ++h) {
+          tc::tma_prefetch_l2_3d(&P.tmap_k, h * 64, kvh, row);
+          tc::tma_prefetch_l2_3d(&P.tmap_v, h * 64, kvh, row);
+        }
+      }
+    }
 #pragma unroll
     for (int j = 0; j < kWin - 1; ++j) win[j] = win[j + 1];
     win[kWin - 1] = it + kWin < my_n ? table_entry(chunk_of(it + kWin)) : -1;
