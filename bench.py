@@ -40,9 +40,7 @@ WORKLOAD = "BASELINE configs[1]: Qwen3-0.6B decode step, bf16, 28 layers, batch 
 # kernel names for the roofline entry and the ncu summaries that measured them
 DECODE_KERNEL_NAMES = {"mma": "paged_decode_mma_kernel", "simt": "paged_decode_kernel",
                        "tcgen05": "paged_decode_tc_kernel", "generic": "attn_generic_kernel"}
-DECODE_PROFILES = {"mma": "decode_mma_qwen3_0.6b_config2.md",
-                   "simt": "decode_simt_qwen3_0.6b_config2.md",
-                   "tcgen05": "decode_tc_qwen3_8b_32k.md"}
+DECODE_PROFILES = {"mma": "decode_mma_qwen3_0.6b_config2.md"}
 
 
 def _peaks():
@@ -382,6 +380,135 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_reference_gpu(args):
+    """The reference's own Triton kernels (baseline/_ref, unmodified) on this GPU.
+
+    A second baseline next to the CPU arm: the same step as the default bench
+    (slot split once, then per layer store_kv + triton_paged_decode, as the
+    reference's CachedAttention runs them), captured in a CUDA graph, plus the
+    configs[4] run (b) decode and the configs[2]/[3] prefill with
+    triton_paged_prefill.  Prints one JSON line; "unavailable" when the
+    reference is not installed.
+    """
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    ref_dir = ROOT / "baseline" / "_ref"
+    if not (ref_dir / "microinfer").is_dir():
+        print(json.dumps({"impl": "reference-gpu", "unavailable": "baseline/_ref not installed"}))
+        return
+    sys.path.insert(0, str(ref_dir))
+    import torch
+    from microinfer.layer.triton_paged_attention import triton_paged_decode, triton_paged_prefill
+    from microinfer.worker.triton_kv_store import store_kv
+
+    from oracle.paged_oracle import decode_bytes, prefill_flops, store_bytes
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, src = _peaks()
+
+    def timed(run, reps):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            run()
+            run()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            run()
+        for _ in range(max(3, args.warmup)):
+            graph.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        del graph
+        return e0.elapsed_time(e1) / reps
+
+    # default workload (configs[1])
+    ctx, table, slots = make_batch(1000, dev)
+    ctx_d, table_d, slots_d = ctx.to(dev), table.to(dev), slots.to(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    kc = torch.empty(LAYERS, NB, BS, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    vc = torch.empty_like(kc).normal_(generator=g)
+    q = torch.randn(LAYERS, NSEQ, HQ, D, generator=g, device=dev).to(torch.bfloat16)
+    kn = torch.randn(LAYERS, NSEQ, HKV, D, generator=g, device=dev).to(torch.bfloat16)
+
+    def step():
+        sl = slots_d.long()
+        blocks = torch.div(sl, BS, rounding_mode="floor")
+        offs = sl - blocks * BS
+        for i in range(LAYERS):
+            store_kv(kc[i], vc[i], blocks, offs, kn[i], kn[i], BS)
+            triton_paged_decode(q[i], kc[i], vc[i], table_d, ctx_d)
+
+    ms = timed(step, args.steps)
+    dec_b, st_b = algorithmic_bytes(ctx.tolist())
+    value = LAYERS * (dec_b + st_b) / (ms * 1e-3) / 1e9
+    del kc, vc
+    # configs[4] run (b): batch 1 at 32768, Qwen3-8B heads, 36 layers
+    layers, hq, ctx_len = 36, 32, 32768
+    nb = ctx_len // BS
+    kc = torch.empty(layers, nb, BS, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+    vc = torch.empty_like(kc).normal_(generator=g)
+    tb = torch.randperm(nb, generator=g, device=dev).to(torch.int32).view(1, nb)
+    cl = torch.tensor([ctx_len], dtype=torch.int32, device=dev)
+    sl1 = (tb[0, -1].long() * BS + BS - 1).view(1)
+    q8 = torch.randn(layers, 1, hq, D, generator=g, device=dev).to(torch.bfloat16)
+    k8 = torch.randn(layers, 1, HKV, D, generator=g, device=dev).to(torch.bfloat16)
+
+    def long_step():
+        blocks = torch.div(sl1, BS, rounding_mode="floor")
+        offs = sl1 - blocks * BS
+        for i in range(layers):
+            store_kv(kc[i], vc[i], blocks, offs, k8[i], k8[i], BS)
+            triton_paged_decode(q8[i], kc[i], vc[i], tb, cl)
+
+    ms_long = timed(long_step, 5)
+    long_b = layers * (decode_bytes([ctx_len], hq, HKV, D, 2, BS) + store_bytes(1, HKV, D, 2))
+    del kc, vc
+    extra = {"long_context_b1": {"ms_per_step": round(ms_long, 4),
+                                 "value": round(long_b / (ms_long * 1e-3) / 1e9, 1), "unit": "GB/s"}}
+    for workload in ("mixed", "prefix"):
+        b = _prefill_batch(workload, dev, None)
+        kc = torch.empty(LAYERS, b["nb"], BS, HKV, D, dtype=torch.bfloat16, device=dev).normal_(generator=g)
+        vc = torch.empty_like(kc).normal_(generator=g)
+        tokens = int(sum(b["q_lens"]))
+        qp = torch.randn(tokens, HQ, D, generator=g, device=dev).to(torch.bfloat16)
+        kp = torch.randn(tokens, HKV, D, generator=g, device=dev).to(torch.bfloat16)
+
+        def prefill_step():
+            sl = b["slots"].long()
+            blocks = torch.div(sl, BS, rounding_mode="floor")
+            offs = sl - blocks * BS
+            for i in range(LAYERS):
+                store_kv(kc[i], vc[i], blocks, offs, kp, kp, BS)
+                triton_paged_prefill(qp, kc[i], vc[i], b["cu_q"], b["cu_k"], b["table"],
+                                     max_seqlen_q=max(b["q_lens"]))
+
+        ms_p = timed(prefill_step, 3)
+        flops = prefill_flops(b["q_lens"], b["contexts"], HQ, D)
+        tf = flops / (ms_p / LAYERS * 1e-3) / 1e12
+        extra[f"prefill_{'mixed' if workload == 'mixed' else 'shared_prefix'}"] = {
+            "us_per_layer": round(ms_p / LAYERS * 1e3, 2), "tflops": round(tf, 1),
+            "tensor_frac": round(tf / peaks["bf16_tflops"], 4)}
+        del kc, vc
+    print(json.dumps({
+        "impl": "reference-gpu", "metric": METRIC, "value": round(value, 2), "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": max(3, args.warmup),
+        "ms_per_step": round(ms, 5), "higher_is_better": True, "dtype": "bf16",
+        "data": "synthetic (seeded torch, BASELINE configs[1] shapes)",
+        "config": {"workload": WORKLOAD, "kernels": "reference Triton store_kv + triton_paged_decode "
+                   "(baseline/_ref, unmodified), CUDA graph"},
+        "frac": round(value / peaks["hbm_gbs"], 4), "peak_source": f"hbm_gbs of {src}",
+        "extra": extra}), flush=True)
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -684,7 +811,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu"], default="ours",
+                    help="reference = the reference's CPU path (oracle port); reference-gpu = "
+                         "its Triton kernels on this GPU (needs baseline/_ref)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", choices=["decode", "long", "prefill", "mixed"], default=None,
                     help="run a small eager case for ncu instead of the benchmark")
@@ -694,6 +823,8 @@ def main():
         run_profile(args)
     elif args.impl == "reference":
         run_reference(args)
+    elif args.impl == "reference-gpu":
+        run_reference_gpu(args)
     else:
         run_ours(args)
 
