@@ -17,9 +17,10 @@
 //   warps 2-5   softmax: one TMEM lane (= query row) per thread; read S with
 //               tcgen05.ld, causal mask (key <= row position), online softmax
 //               in the log2 domain with lazy rescale of O (only when the row
-//               max grows by more than 2^8), write P as fp16/bf16 into the
-//               128-byte-swizzled shared tile the next MMA reads; epilogue
-//               O / l -> global.
+//               max grows by more than 2^8), write P as fp16/bf16 into one of
+//               two 128-byte-swizzled shared tiles (P is double-buffered, so
+//               the softmax of tile j waits on P.V(j-1) only to rescale O);
+//               epilogue O / l -> global.
 //
 // Shared memory operands use the SWIZZLE_128B canonical layout (8 rows x 128
 // bytes atoms); a 128x128 16-bit tile is two 16 KB column halves.  TMEM: S0
@@ -68,8 +69,8 @@ constexpr int kHalf = 16384;
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTileBytes;      // 2 stages
 constexpr int kOffV = kOffK + 2 * kTileBytes;  // 2 stages
-constexpr int kOffP = kOffV + 2 * kTileBytes;
-constexpr int kOffBar = kOffP + kTileBytes;
+constexpr int kOffP = kOffV + 2 * kTileBytes;  // 2 buffers
+constexpr int kOffBar = kOffP + 2 * kTileBytes;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + TMEM slot + alignment slack
 constexpr uint32_t kTmemCols = 512;
 
@@ -82,10 +83,10 @@ enum {
   B_VEMPTY = 7,  // +stage
   B_SFULL = 9,   // +buffer
   B_SEMPTY = 11, // +buffer
-  B_PFULL = 13,
-  B_ODONE = 14,
-  B_FIN = 15,
-  B_COUNT = 16
+  B_PFULL = 13,  // +P buffer
+  B_ODONE = 15,  // +P buffer: P.V of the tiles using that buffer done
+  B_FIN = 17,
+  B_COUNT = 18
 };
 
 // K-major SW128 descriptor of 16-element K-step `kk` of a 128 x 128 tile.
@@ -161,8 +162,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       mbar_init(&bar[B_SFULL + s], 1);
       mbar_init(&bar[B_SEMPTY + s], 128);
     }
-    mbar_init(&bar[B_PFULL], 128);
-    mbar_init(&bar[B_ODONE], 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar[B_PFULL + b], 128);
+      mbar_init(&bar[B_ODONE + b], 1);
+    }
     mbar_init(&bar[B_FIN], 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -236,15 +239,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     if (lane == 0) {
       bool ok = mbar_wait_bounded(&bar[B_Q], 0, p.status);
       auto pv = [&](int jj) -> bool {
-        const int s = jj & 1;
-        if (!mbar_wait_bounded(&bar[B_PFULL], jj & 1, p.status)) return false;
+        const int s = jj & 1;  // V stage and P buffer
+        if (!mbar_wait_bounded(&bar[B_PFULL + s], (jj >> 1) & 1, p.status)) return false;
         if (!mbar_wait_bounded(&bar[B_VFULL + s], (jj >> 1) & 1, p.status)) return false;
         tc::fence_after_sync();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          tc::umma_f16(tO, kmajor_desc(sP, kk), mnmajor_desc(sV + s * kTileBytes, kk), kIdescPV,
-                       (jj > 0 || kk > 0) ? 1u : 0u);
-        tc::umma_commit(&bar[B_ODONE]);
+          tc::umma_f16(tO, kmajor_desc(sP + s * kTileBytes, kk), mnmajor_desc(sV + s * kTileBytes, kk),
+                       kIdescPV, (jj > 0 || kk > 0) ? 1u : 0u);
+        tc::umma_commit(&bar[B_ODONE + s]);
         tc::umma_commit(&bar[B_VEMPTY + s]);
         return true;
       };
@@ -278,7 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const bool rvalid = tok < nt;
     const int pos = prefix + t0 + tok;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    uint8_t *prow = smem + kOffP + r * 128;
+    uint8_t *prow0 = smem + kOffP + r * 128;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
@@ -303,12 +306,28 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       mbar_arrive(&bar[B_SEMPTY + s]);
 
       const int lim = rvalid ? pos - j * 128 : -1;  // key c of this tile visible iff c <= lim
-      float mx = -INFINITY;
+      // Raw scores stay unscaled: the scale is folded into the FFMA feeding
+      // ex2 below.  Masked keys get the value that scales to -inf.
+      const float sl2 = p.scale_log2;
+      const bool pos_scale = sl2 >= 0.f;
+      if (lim < 127) {  // diagonal tile (or an invalid row): mask keys after the position
+        const float masked = pos_scale ? -INFINITY : INFINITY;
 #pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        x[c] = c <= lim ? x[c] * p.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, x[c]);
+        for (int c = 0; c < 128; ++c) x[c] = c <= lim ? x[c] : masked;
       }
+      float r4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) r4[i] = pos_scale ? -INFINITY : INFINITY;
+      if (pos_scale) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) r4[c & 3] = fmaxf(r4[c & 3], x[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) r4[c & 3] = fminf(r4[c & 3], x[c]);
+      }
+      const float best = pos_scale ? fmaxf(fmaxf(r4[0], r4[1]), fmaxf(r4[2], r4[3]))
+                                   : fminf(fminf(r4[0], r4[1]), fminf(r4[2], r4[3]));
+      const float mx = lim < 0 ? -INFINITY : best * sl2;  // this tile's row max, log2 domain
       float m_new = m, alpha = 1.f;
       bool rescale = false;
       if (mx > m + 8.f) {
@@ -316,15 +335,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         rescale = m != -INFINITY;
         alpha = rescale ? fast_exp2(m - m_new) : 0.f;
       }
-      // P_{j-1} must be consumed (and O settled) before P_j / O are touched.
-      if (j >= 1) {
-        good = mbar_wait_bounded(&bar[B_ODONE], (j - 1) & 1, p.status);
+      // P buffer j%2 is free once P.V(j-2) is done; rescaling O needs P.V(j-1).
+      const bool need_p = j >= 2, need_r = j >= 1 && __any_sync(0xffffffffu, rescale);
+      if (need_p || need_r) {
+        good = 1;
+        if (need_p) good &= mbar_wait_bounded(&bar[B_ODONE + (j & 1)], ((j - 2) >> 1) & 1, p.status);
+        if (need_r) good &= mbar_wait_bounded(&bar[B_ODONE + ((j - 1) & 1)], ((j - 1) >> 1) & 1, p.status);
         if (!__all_sync(0xffffffffu, good)) {
           ok = false;
           break;
         }
         tc::fence_after_sync();
-        if (__any_sync(0xffffffffu, rescale)) {
+        if (need_r) {
           const float a = rescale ? alpha : 1.f;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -338,15 +360,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           tc::tmem_wait_st();
         }
       }
-      float rs = 0.f;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      const float nb = m_new == -INFINITY ? 0.f : -m_new;  // masked: ex2(-inf) = 0
+      uint8_t *prow = prow0 + s * kTileBytes;
 #pragma unroll
       for (int c8 = 0; c8 < 16; ++c8) {
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const float xv = x[c8 * 8 + i];
-          e[i] = xv == -INFINITY ? 0.f : fast_exp2(xv - m_new);
-          rs += e[i];
+          e[i] = fast_exp2(fmaf(x[c8 * 8 + i], sl2, nb));
+          rs4[i & 3] += e[i];
         }
         uint4 w;
         w.x = pack2(e[0], e[1], kBf16);
@@ -356,14 +379,14 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         const int half = c8 >> 3, chunk = c8 & 7;
         *reinterpret_cast<uint4 *>(prow + half * kHalf + ((chunk ^ (r & 7)) << 4)) = w;
       }
-      l = l * alpha + rs;
+      l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
       m = m_new;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
       tc::fence_before_sync();
-      mbar_arrive(&bar[B_PFULL]);
+      mbar_arrive(&bar[B_PFULL + s]);
     }
     if (ok) {
-      const int good = mbar_wait_bounded(&bar[B_ODONE], (nkv - 1) & 1, p.status);
+      const int good = mbar_wait_bounded(&bar[B_ODONE + ((nkv - 1) & 1)], ((nkv - 1) >> 1) & 1, p.status);
       ok = __all_sync(0xffffffffu, good);
     }
     if (ok) {
