@@ -3,24 +3,27 @@
 // Work tile: 128 query rows = (TQ = 128/G tokens) x (G query heads of one kv
 // head), against every cached key of the sequence up to the tile's last
 // position, in 128-key tiles.  One CTA per (query tile, kv head, sequence);
-// 192 threads in three roles:
+// 352 threads in four roles:
 //
-//   warp 0      TMA producer: Q once (two 64-column halves, 3-D map over
-//               [tokens, Hq, D]), then per key tile 8 groups of 16 keys for
-//               K and for V (3-D map over [slots, Hkv, D]); each group's slot
-//               comes from the block table, groups past the context load from
-//               an out-of-range coordinate (zero fill).  K/V ring of 2 stages.
+//   warps 0,10  TMA producers: warp 0 Q once (two 64-column halves, 3-D map
+//               over [tokens, Hq, D]) and the K tiles, warp 10 the V tiles: per
+//               key tile 8 groups of 16 keys (3-D map over [slots, Hkv, D]);
+//               each group's slot comes from the block table (looked up one
+//               tile ahead), groups past the context load from an out-of-range
+//               coordinate (zero fill).  K and V rings of 2 stages each.
 //   warp 1      TMEM owner and single-thread MMA issuer:
 //                 S[j%2] = Q K_j^T   (M=128, N=128, K=D; A, B K-major)
 //                 O     += P_j V_j   (M=128, N=D,   K=128; B MN-major)
 //               S is double-buffered so S_{j+1} overlaps the softmax of S_j.
-//   warps 2-5   softmax: one TMEM lane (= query row) per thread; read S with
-//               tcgen05.ld, causal mask (key <= row position), online softmax
-//               in the log2 domain with lazy rescale of O (only when the row
-//               max grows by more than 2^8), write P as fp16/bf16 into one of
-//               two 128-byte-swizzled shared tiles (P is double-buffered, so
-//               the softmax of tile j waits on P.V(j-1) only to rescale O);
-//               epilogue O / l -> global.
+//   warps 2-9   softmax, two warpgroups: TMEM lane (= query row) per thread,
+//               warps 2-5 columns 0-63 and warps 6-9 columns 64-127 of the
+//               row; read S with tcgen05.ld, causal mask only on diagonal
+//               tiles, online softmax in the log2 domain (scale folded into
+//               the FFMA feeding ex2) with lazy rescale of O (only when the
+//               row max grows by more than 2^8); the row halves combine their
+//               maxima at one barrier per tile; P as fp16/bf16 into the
+//               128-byte-swizzled shared tile the next MMA reads; epilogue
+//               O / l -> global.
 //
 // Shared memory operands use the SWIZZLE_128B canonical layout (8 rows x 128
 // bytes atoms); a 128x128 16-bit tile is two 16 KB column halves.  TMEM: S0
@@ -63,14 +66,15 @@ struct __align__(64) PrefillTcParams {
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 352;
 constexpr int kTileBytes = 32768;  // 128 x 128 x 16-bit
 constexpr int kHalf = 16384;
 constexpr int kOffQ = 0;
 constexpr int kOffK = kOffQ + kTileBytes;      // 2 stages
 constexpr int kOffV = kOffK + 2 * kTileBytes;  // 2 stages
-constexpr int kOffP = kOffV + 2 * kTileBytes;  // 2 buffers
-constexpr int kOffBar = kOffP + 2 * kTileBytes;
+constexpr int kOffP = kOffV + 2 * kTileBytes;
+constexpr int kOffRed = kOffP + kTileBytes;  // [2][2][128] floats: the row halves' maxima / sums
+constexpr int kOffBar = kOffRed + 2048;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + TMEM slot + alignment slack
 constexpr uint32_t kTmemCols = 512;
 
@@ -105,6 +109,19 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   }
   __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// Barrier over the 8 softmax warps (id 1, 256 threads) that also ORs `bad`,
+// so every softmax warp takes the same exit.
+__device__ __forceinline__ bool softmax_pair_sync_any(bool bad) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pin, pout;\n\tsetp.ne.u32 pin, %1, 0;\n\t"
+      "bar.red.or.pred pout, 1, 256, pin;\n\tselp.u32 %0, 1, 0, pout;\n\t}"
+      : "=r"(r)
+      : "r"(bad ? 1u : 0u)
+      : "memory");
+  return r != 0;
 }
 
 }  // namespace
@@ -160,10 +177,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       mbar_init(&bar[B_KEMPTY + s], 1);
       mbar_init(&bar[B_VEMPTY + s], 1);
       mbar_init(&bar[B_SFULL + s], 1);
-      mbar_init(&bar[B_SEMPTY + s], 128);
+      mbar_init(&bar[B_SEMPTY + s], 256);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&bar[B_PFULL + b], 128);
+      mbar_init(&bar[B_PFULL + b], 256);
       mbar_init(&bar[B_ODONE + b], 1);
     }
     mbar_init(&bar[B_FIN], 1);
@@ -177,8 +194,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   const uint32_t tmem = *tmem_slot;
   const uint32_t tS = tmem, tO = tmem + 256;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------ producer
+  if (warp == 0 || warp == 10) {
+    // ---------------------------------------------------------- producers
+    // warp 0 loads Q and the K tiles, warp 10 the V tiles, so a K load never
+    // waits behind the (later) release of a V stage.  Each warp looks up the
+    // next tile's pages while it waits for the current stage.
+    const bool is_v = warp == 10;
     const int32_t *table = p.block_tables + seq * p.bt_stride;
     auto kv_row = [&](int key0) -> int {
       if (key0 >= ctx) return static_cast<int>(p.kv_rows);  // past the context: zero fill
@@ -192,47 +213,45 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       return static_cast<int>(blk * p.block_size + key0 % p.block_size);
     };
     bool ok = true;
-    int kv_armed = 0;  // key tiles whose loads were issued
+    int armed = 0;  // key tiles whose loads were issued
     if (lane == 0) {
-      tc::prefetch_tmap(&p.tmap_q);
-      tc::prefetch_tmap(&p.tmap_k);
-      tc::prefetch_tmap(&p.tmap_v);
-      mbar_arrive_expect_tx(&bar[B_Q], 2 * kHalf);
-      for (int dh = 0; dh < 2; ++dh)
-        tc::tma_load_3d(smem + kOffQ + dh * kHalf, &p.tmap_q, dh * 64, kvh * G, q_start + t0, &bar[B_Q]);
+      tc::prefetch_tmap(is_v ? &p.tmap_v : &p.tmap_k);
+      if (!is_v) {
+        tc::prefetch_tmap(&p.tmap_q);
+        mbar_arrive_expect_tx(&bar[B_Q], 2 * kHalf);
+        for (int dh = 0; dh < 2; ++dh)
+          tc::tma_load_3d(smem + kOffQ + dh * kHalf, &p.tmap_q, dh * 64, kvh * G, q_start + t0, &bar[B_Q]);
+      }
     }
+    // lanes 0..15 each load one (16-key group, 64-column half) box
+    const int g = lane >> 1, dh = lane & 1;
+    const CUtensorMap *map = is_v ? &p.tmap_v : &p.tmap_k;
+    uint8_t *ring = smem + (is_v ? kOffV : kOffK);
+    int row = lane < 16 ? kv_row(g * 16) : 0;
     for (int j = 0; j < nkv && ok; ++j) {
       const int s = j & 1;
-      const uint32_t empty_parity = ((j >> 1) & 1) ^ 1;
-      // lanes 0..15 each load one (16-key group, 64-column half) box
-      const int g = lane >> 1, dh = lane & 1;
-      const int row = lane < 16 ? kv_row(j * 128 + g * 16) : 0;
-      for (int kv = 0; kv < 2 && ok; ++kv) {
-        uint64_t *empty = &bar[(kv ? B_VEMPTY : B_KEMPTY) + s];
-        uint64_t *full = &bar[(kv ? B_VFULL : B_KFULL) + s];
-        int good = 1;
-        if (lane == 0) good = mbar_wait_bounded(empty, empty_parity, p.status) && !*(volatile int *)abort_flag;
-        good = __shfl_sync(0xffffffffu, good, 0);
-        if (!good) {
-          ok = false;
-          break;
-        }
-        if (lane == 0) mbar_arrive_expect_tx(full, kTileBytes);
-        __syncwarp();
-        if (lane < 16)
-          tc::tma_load_3d(smem + (kv ? kOffV : kOffK) + s * kTileBytes + dh * kHalf + g * 2048,
-                          kv ? &p.tmap_v : &p.tmap_k, dh * 64, kvh, row, full);
+      const int next_row = (lane < 16 && j + 1 < nkv) ? kv_row((j + 1) * 128 + g * 16) : 0;
+      uint64_t *empty = &bar[(is_v ? B_VEMPTY : B_KEMPTY) + s];
+      uint64_t *full = &bar[(is_v ? B_VFULL : B_KFULL) + s];
+      int good = 1;
+      if (lane == 0) good = mbar_wait_bounded(empty, ((j >> 1) & 1) ^ 1, p.status) && !*(volatile int *)abort_flag;
+      good = __shfl_sync(0xffffffffu, good, 0);
+      if (!good) {
+        ok = false;
+        break;
       }
-      if (ok) kv_armed = j + 1;
+      if (lane == 0) mbar_arrive_expect_tx(full, kTileBytes);
+      __syncwarp();
+      if (lane < 16) tc::tma_load_3d(ring + s * kTileBytes + dh * kHalf + g * 2048, map, dh * 64, kvh, row, full);
+      armed = j + 1;
+      row = next_row;
     }
     if (!ok) {
       if (lane == 0) *(volatile int *)abort_flag = 1;
       // Let this CTA's own loads in flight land before its shared memory goes away.
       if (lane == 0)
-        for (int j = max(0, kv_armed - 2); j < kv_armed; ++j) {
-          mbar_wait_bounded(&bar[B_KFULL + (j & 1)], (j >> 1) & 1, p.status);
-          mbar_wait_bounded(&bar[B_VFULL + (j & 1)], (j >> 1) & 1, p.status);
-        }
+        for (int j = max(0, armed - 2); j < armed; ++j)
+          mbar_wait_bounded(&bar[(is_v ? B_VFULL : B_KFULL) + (j & 1)], (j >> 1) & 1, p.status);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -245,8 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         tc::fence_after_sync();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          tc::umma_f16(tO, kmajor_desc(sP + s * kTileBytes, kk), mnmajor_desc(sV + s * kTileBytes, kk),
-                       kIdescPV, (jj > 0 || kk > 0) ? 1u : 0u);
+          tc::umma_f16(tO, kmajor_desc(sP, kk), mnmajor_desc(sV + s * kTileBytes, kk), kIdescPV,
+                       (jj > 0 || kk > 0) ? 1u : 0u);
         tc::umma_commit(&bar[B_ODONE + s]);
         tc::umma_commit(&bar[B_VEMPTY + s]);
         return true;
@@ -275,59 +294,72 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
+    // Two warpgroups: warps 2-5 take columns 0-63 of every row, warps 6-9
+    // columns 64-127 (a warp reaches the TMEM lanes 32 * (warp % 4) ...).  The
+    // two halves of a row exchange their partial max once per tile through
+    // shared memory at a 256-thread barrier that also ORs an abort flag.
     const int q4 = warp & 3;
-    const int r = q4 * 32 + lane;  // TMEM lane = query row of the tile
+    const int hc = warp >= 6 ? 1 : 0;  // column half
+    const int r = q4 * 32 + lane;      // TMEM lane = query row of the tile
     const int tok = r / G;
     const bool rvalid = tok < nt;
     const int pos = prefix + t0 + tok;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    uint8_t *prow0 = smem + kOffP + r * 128;
-    float m = -INFINITY, l = 0.f;
-    bool ok = true;
+    uint8_t *prow = smem + kOffP + hc * kHalf + r * 128;
+    float *red = reinterpret_cast<float *>(smem + kOffRed);  // [2 parity][2 half][128 rows]
+    const float sl2 = p.scale_log2;
+    const bool pos_scale = sl2 >= 0.f;
+    float m = -INFINITY, l = 0.f;  // l: this half's share of the row sum
+    bool ok = true, bad = false;
     for (int j = 0; j < nkv; ++j) {
       const int s = j & 1;
-      int good = mbar_wait_bounded(&bar[B_SFULL + s], (j >> 1) & 1, p.status) &&
-                 !*(volatile int *)abort_flag;
-      if (!__all_sync(0xffffffffu, good)) {
-        ok = false;
-        break;
-      }
-      tc::fence_after_sync();
-      float x[128];
+      const bool got = mbar_wait_bounded(&bar[B_SFULL + s], (j >> 1) & 1, p.status) &&
+                       !*(volatile int *)abort_flag;
+      float x[64];
+      if (got) {
+        tc::fence_after_sync();
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tc::tmem_ld32(tS + s * 128 + lane_off + c * 32, v);
+        for (int c = 0; c < 2; ++c) {
+          float v[32];
+          tc::tmem_ld32(tS + s * 128 + hc * 64 + lane_off + c * 32, v);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[c * 32 + i] = v[i];
+          for (int i = 0; i < 32; ++i) x[c * 32 + i] = v[i];
+        }
+        tc::tmem_wait_ld();
+        tc::fence_before_sync();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) x[i] = 0.f;
       }
-      tc::tmem_wait_ld();
-      tc::fence_before_sync();
       mbar_arrive(&bar[B_SEMPTY + s]);
+      bad |= !got;
 
-      const int lim = rvalid ? pos - j * 128 : -1;  // key c of this tile visible iff c <= lim
-      // Raw scores stay unscaled: the scale is folded into the FFMA feeding
-      // ex2 below.  Masked keys get the value that scales to -inf.
-      const float sl2 = p.scale_log2;
-      const bool pos_scale = sl2 >= 0.f;
-      if (lim < 127) {  // diagonal tile (or an invalid row): mask keys after the position
+      // key c of this half is visible iff hc * 64 + c <= pos - j * 128
+      const int lim = rvalid ? pos - j * 128 - hc * 64 : -1;
+      if (lim < 63) {
         const float masked = pos_scale ? -INFINITY : INFINITY;
 #pragma unroll
-        for (int c = 0; c < 128; ++c) x[c] = c <= lim ? x[c] : masked;
+        for (int c = 0; c < 64; ++c) x[c] = c <= lim ? x[c] : masked;
       }
       float r4[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) r4[i] = pos_scale ? -INFINITY : INFINITY;
       if (pos_scale) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) r4[c & 3] = fmaxf(r4[c & 3], x[c]);
+        for (int c = 0; c < 64; ++c) r4[c & 3] = fmaxf(r4[c & 3], x[c]);
       } else {
 #pragma unroll
-        for (int c = 0; c < 128; ++c) r4[c & 3] = fminf(r4[c & 3], x[c]);
+        for (int c = 0; c < 64; ++c) r4[c & 3] = fminf(r4[c & 3], x[c]);
       }
       const float best = pos_scale ? fmaxf(fmaxf(r4[0], r4[1]), fmaxf(r4[2], r4[3]))
                                    : fminf(fminf(r4[0], r4[1]), fminf(r4[2], r4[3]));
-      const float mx = lim < 0 ? -INFINITY : best * sl2;  // this tile's row max, log2 domain
+      const float hmx = lim < 0 ? -INFINITY : best * sl2;  // this half's max, log2 domain
+      red[(s * 2 + hc) * 128 + r] = hmx;
+      if (softmax_pair_sync_any(bad)) {  // also publishes the halves' maxima
+        ok = false;
+        break;
+      }
+      const float mx = fmaxf(hmx, red[(s * 2 + (hc ^ 1)) * 128 + r]);
       float m_new = m, alpha = 1.f;
       bool rescale = false;
       if (mx > m + 8.f) {
@@ -335,36 +367,30 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         rescale = m != -INFINITY;
         alpha = rescale ? fast_exp2(m - m_new) : 0.f;
       }
-      // P buffer j%2 is free once P.V(j-2) is done; rescaling O needs P.V(j-1).
-      const bool need_p = j >= 2, need_r = j >= 1 && __any_sync(0xffffffffu, rescale);
-      if (need_p || need_r) {
-        good = 1;
-        if (need_p) good &= mbar_wait_bounded(&bar[B_ODONE + (j & 1)], ((j - 2) >> 1) & 1, p.status);
-        if (need_r) good &= mbar_wait_bounded(&bar[B_ODONE + ((j - 1) & 1)], ((j - 1) >> 1) & 1, p.status);
-        if (!__all_sync(0xffffffffu, good)) {
-          ok = false;
-          break;
-        }
+      // The single P buffer and O are free once P.V(j-1) is done.
+      if (j >= 1) {
+        const bool done = mbar_wait_bounded(&bar[B_ODONE + ((j - 1) & 1)], ((j - 1) >> 1) & 1,
+                                            p.status);
+        bad |= !done;  // acted on at the next barrier; the writes below stay in bounds
         tc::fence_after_sync();
-        if (need_r) {
+        if (__any_sync(0xffffffffu, rescale)) {
           const float a = rescale ? alpha : 1.f;
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
             float o[32];
-            tc::tmem_ld32(tO + lane_off + c * 32, o);
+            tc::tmem_ld32(tO + hc * 64 + lane_off + c * 32, o);
             tc::tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= a;
-            tc::tmem_st32(tO + lane_off + c * 32, o);
+            tc::tmem_st32(tO + hc * 64 + lane_off + c * 32, o);
           }
           tc::tmem_wait_st();
         }
       }
       float rs4[4] = {0.f, 0.f, 0.f, 0.f};
       const float nb = m_new == -INFINITY ? 0.f : -m_new;  // masked: ex2(-inf) = 0
-      uint8_t *prow = prow0 + s * kTileBytes;
 #pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
+      for (int c8 = 0; c8 < 8; ++c8) {
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -376,8 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         w.y = pack2(e[2], e[3], kBf16);
         w.z = pack2(e[4], e[5], kBf16);
         w.w = pack2(e[6], e[7], kBf16);
-        const int half = c8 >> 3, chunk = c8 & 7;
-        *reinterpret_cast<uint4 *>(prow + half * kHalf + ((chunk ^ (r & 7)) << 4)) = w;
+        *reinterpret_cast<uint4 *>(prow + ((c8 ^ (r & 7)) << 4)) = w;
       }
       l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
       m = m_new;
@@ -385,18 +410,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       tc::fence_before_sync();
       mbar_arrive(&bar[B_PFULL + s]);
     }
+    // Row sum of both halves; the barrier also settles a pending abort.
     if (ok) {
+      red[((nkv & 1) * 2 + hc) * 128 + r] = l;
+      ok = !softmax_pair_sync_any(bad);
+    }
+    float L = 0.f;
+    if (ok) {
+      L = l + red[((nkv & 1) * 2 + (hc ^ 1)) * 128 + r];
       const int good = mbar_wait_bounded(&bar[B_ODONE + ((nkv - 1) & 1)], ((nkv - 1) >> 1) & 1, p.status);
       ok = __all_sync(0xffffffffu, good);
     }
     if (ok) {
       tc::fence_after_sync();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      T *orow = out + (static_cast<int64_t>(q_start + t0 + tok) * p.num_q_heads + kvh * G + r % G) * 128;
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      T *orow = out + (static_cast<int64_t>(q_start + t0 + tok) * p.num_q_heads + kvh * G + r % G) * 128 +
+                hc * 64;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float o[32];
-        tc::tmem_ld32(tO + lane_off + c * 32, o);
+        tc::tmem_ld32(tO + hc * 64 + lane_off + c * 32, o);
         tc::tmem_wait_ld();
         if (rvalid) {
 #pragma unroll
