@@ -8,9 +8,10 @@
 //   warps 0,10  TMA producers: warp 0 Q once (two 64-column halves, 3-D map
 //               over [tokens, Hq, D]) and the K tiles, warp 10 the V tiles: per
 //               key tile 8 groups of 16 keys (3-D map over [slots, Hkv, D]);
-//               each group's slot comes from the block table (looked up one
-//               tile ahead), groups past the context load from an out-of-range
-//               coordinate (zero fill).  K and V rings of 2 stages each.
+//               each group's slot comes from the block table (looked up in
+//               batches of 4 tiles, one batch ahead), groups past the context
+//               load from an out-of-range
+//               coordinate (zero fill).  K ring of 3 stages, V ring of 2.
 //   warp 1      TMEM owner and single-thread MMA issuer:
 //                 S[j%2] = Q K_j^T   (M=128, N=128, K=D; A, B K-major)
 //                 O     += P_j V_j   (M=128, N=D,   K=128; B MN-major)
@@ -21,13 +22,14 @@
 //               tiles, online softmax in the log2 domain (scale folded into
 //               the FFMA feeding ex2) with lazy rescale of O (only when the
 //               row max grows by more than 2^8); the row halves combine their
-//               maxima at one barrier per tile; P as fp16/bf16 into the
+//               maxima through TMEM columns 384-387 at one barrier per tile;
+//               P as fp16/bf16 into the
 //               128-byte-swizzled shared tile the next MMA reads; epilogue
 //               O / l -> global.
 //
 // Shared memory operands use the SWIZZLE_128B canonical layout (8 rows x 128
 // bytes atoms); a 128x128 16-bit tile is two 16 KB column halves.  TMEM: S0
-// at column 0, S1 at 128, O at 256 (512 columns allocated).
+// at column 0, S1 at 128, O at 256, softmax exchange at 384 (512 allocated).
 //
 // Dense mode (no block table) reads K/V rows cu_seqlens_k[s] + key of a
 // contiguous [tokens, Hkv, D] tensor: the no-prefix ("direct") prefill.
@@ -70,27 +72,28 @@ constexpr int kThreads = 352;
 constexpr int kTileBytes = 32768;  // 128 x 128 x 16-bit
 constexpr int kHalf = 16384;
 constexpr int kOffQ = 0;
-constexpr int kOffK = kOffQ + kTileBytes;      // 2 stages
-constexpr int kOffV = kOffK + 2 * kTileBytes;  // 2 stages
-constexpr int kOffP = kOffV + 2 * kTileBytes;
-constexpr int kOffRed = kOffP + kTileBytes;  // [2][2][128] floats: the row halves' maxima / sums
-constexpr int kOffBar = kOffRed + 2048;
+constexpr int kKStages = 3;  // K is released after S (early), so it runs deeper than V
+constexpr int kVStages = 2;
+constexpr int kOffK = kOffQ + kTileBytes;
+constexpr int kOffV = kOffK + kKStages * kTileBytes;
+constexpr int kOffP = kOffV + kVStages * kTileBytes;
+constexpr int kOffBar = kOffP + kTileBytes;
 constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + TMEM slot + alignment slack
 constexpr uint32_t kTmemCols = 512;
 
 // barrier indices
 enum {
   B_Q = 0,
-  B_KFULL = 1,   // +stage
-  B_VFULL = 3,   // +stage
-  B_KEMPTY = 5,  // +stage
-  B_VEMPTY = 7,  // +stage
-  B_SFULL = 9,   // +buffer
-  B_SEMPTY = 11, // +buffer
-  B_PFULL = 13,  // +P buffer
-  B_ODONE = 15,  // +P buffer: P.V of the tiles using that buffer done
-  B_FIN = 17,
-  B_COUNT = 18
+  B_KFULL = 1,    // +K stage (3)
+  B_VFULL = 4,    // +V stage (2)
+  B_KEMPTY = 6,   // +K stage
+  B_VEMPTY = 9,   // +V stage
+  B_SFULL = 11,   // +S buffer (2)
+  B_SEMPTY = 13,  // +S buffer
+  B_PFULL = 15,   // +tile parity
+  B_ODONE = 17,   // +tile parity: P.V of the tiles with that parity done
+  B_FIN = 19,
+  B_COUNT = 20
 };
 
 // K-major SW128 descriptor of 16-element K-step `kk` of a 128 x 128 tile.
@@ -171,11 +174,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
 
   if (threadIdx.x == 0) {
     mbar_init(&bar[B_Q], 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(&bar[B_KFULL + s], 1);
-      mbar_init(&bar[B_VFULL + s], 1);
       mbar_init(&bar[B_KEMPTY + s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&bar[B_VFULL + s], 1);
       mbar_init(&bar[B_VEMPTY + s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&bar[B_SFULL + s], 1);
       mbar_init(&bar[B_SEMPTY + s], 256);
     }
@@ -201,16 +208,21 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     // next tile's pages while it waits for the current stage.
     const bool is_v = warp == 10;
     const int32_t *table = p.block_tables + seq * p.bt_stride;
-    auto kv_row = [&](int key0) -> int {
+    // Raw table entry for a 16-key group (loads only, so several can be in
+    // flight); validated and turned into a row when the group is loaded.
+    auto kv_entry = [&](int key0) -> int {
+      if (key0 >= ctx || !p.paged) return 0;
+      const int64_t col = key0 / p.block_size;
+      return col < p.bt_stride ? __ldg(table + col) : -1;
+    };
+    auto kv_row = [&](int key0, int entry) -> int {
       if (key0 >= ctx) return static_cast<int>(p.kv_rows);  // past the context: zero fill
       if (!p.paged) return kv0 + key0;
-      const int64_t col = key0 / p.block_size;
-      const int64_t blk = col < p.bt_stride ? table[col] : -1;
-      if (blk < 0 || blk >= p.num_blocks) {
+      if (entry < 0 || entry >= p.num_blocks) {
         flag_status(p.status, MI_DEV_BAD_BLOCK);
         return static_cast<int>(p.kv_rows);
       }
-      return static_cast<int>(blk * p.block_size + key0 % p.block_size);
+      return static_cast<int>(static_cast<int64_t>(entry) * p.block_size + key0 % p.block_size);
     };
     bool ok = true;
     int armed = 0;  // key tiles whose loads were issued
@@ -225,33 +237,45 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     }
     // lanes 0..15 each load one (16-key group, 64-column half) box
     const int g = lane >> 1, dh = lane & 1;
+    const int nst = is_v ? kVStages : kKStages;
     const CUtensorMap *map = is_v ? &p.tmap_v : &p.tmap_k;
     uint8_t *ring = smem + (is_v ? kOffV : kOffK);
-    int row = lane < 16 ? kv_row(g * 16) : 0;
+    const int full0 = is_v ? B_VFULL : B_KFULL, empty0 = is_v ? B_VEMPTY : B_KEMPTY;
+    // Page lookups in batches of 4 tiles: lane (t, b) of the warp holds the
+    // table entry of group b of tile 4k + t; the next batch is loaded a whole
+    // batch ahead, and a shuffle hands each copy lane its entry, so no
+    // register move ever waits on a recent load.
+    const int bt = lane >> 3, bg = lane & 7;
+    auto entry_for = [&](int tile) { return tile < nkv ? kv_entry(tile * 128 + bg * 16) : 0; };
+    int cur = entry_for(bt), nxt = entry_for(4 + bt);
     for (int j = 0; j < nkv && ok; ++j) {
-      const int s = j & 1;
-      const int next_row = (lane < 16 && j + 1 < nkv) ? kv_row((j + 1) * 128 + g * 16) : 0;
-      uint64_t *empty = &bar[(is_v ? B_VEMPTY : B_KEMPTY) + s];
-      uint64_t *full = &bar[(is_v ? B_VFULL : B_KFULL) + s];
+      const int s = j % nst;
+      const uint32_t empty_parity = ((j / nst) & 1) ^ 1;
+      if (j > 0 && (j & 3) == 0) {
+        cur = nxt;
+        nxt = entry_for(j + 4 + bt);
+      }
+      const int entry = __shfl_sync(0xffffffffu, cur, ((j & 3) * 8 + g) & 31);
+      const int row = lane < 16 ? kv_row(j * 128 + g * 16, entry) : 0;
       int good = 1;
-      if (lane == 0) good = mbar_wait_bounded(empty, ((j >> 1) & 1) ^ 1, p.status) && !*(volatile int *)abort_flag;
+      if (lane == 0) good = mbar_wait_bounded(&bar[empty0 + s], empty_parity, p.status) && !*(volatile int *)abort_flag;
       good = __shfl_sync(0xffffffffu, good, 0);
       if (!good) {
         ok = false;
         break;
       }
-      if (lane == 0) mbar_arrive_expect_tx(full, kTileBytes);
+      if (lane == 0) mbar_arrive_expect_tx(&bar[full0 + s], kTileBytes);
       __syncwarp();
-      if (lane < 16) tc::tma_load_3d(ring + s * kTileBytes + dh * kHalf + g * 2048, map, dh * 64, kvh, row, full);
+      if (lane < 16)
+        tc::tma_load_3d(ring + s * kTileBytes + dh * kHalf + g * 2048, map, dh * 64, kvh, row, &bar[full0 + s]);
       armed = j + 1;
-      row = next_row;
     }
     if (!ok) {
       if (lane == 0) *(volatile int *)abort_flag = 1;
       // Let this CTA's own loads in flight land before its shared memory goes away.
       if (lane == 0)
-        for (int j = max(0, armed - 2); j < armed; ++j)
-          mbar_wait_bounded(&bar[(is_v ? B_VFULL : B_KFULL) + (j & 1)], (j >> 1) & 1, p.status);
+        for (int j = max(0, armed - nst); j < armed; ++j)
+          mbar_wait_bounded(&bar[full0 + j % nst], (j / nst) & 1, p.status);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -271,18 +295,18 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
         return true;
       };
       for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j & 1;
-        ok = mbar_wait_bounded(&bar[B_KFULL + s], (j >> 1) & 1, p.status) &&
+        const int s = j & 1, ks = j % kKStages;
+        ok = mbar_wait_bounded(&bar[B_KFULL + ks], (j / kKStages) & 1, p.status) &&
              mbar_wait_bounded(&bar[B_SEMPTY + s], ((j >> 1) & 1) ^ 1, p.status) &&
              !*(volatile int *)abort_flag;
         if (!ok) break;
         tc::fence_after_sync();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          tc::umma_f16(tS + s * 128, kmajor_desc(sQ, kk), kmajor_desc(sK + s * kTileBytes, kk),
+          tc::umma_f16(tS + s * 128, kmajor_desc(sQ, kk), kmajor_desc(sK + ks * kTileBytes, kk),
                        kIdescQK, kk > 0 ? 1u : 0u);
         tc::umma_commit(&bar[B_SFULL + s]);
-        tc::umma_commit(&bar[B_KEMPTY + s]);
+        tc::umma_commit(&bar[B_KEMPTY + ks]);
         if (j >= 1) ok = pv(j - 1);
       }
       if (ok) ok = pv(nkv - 1);
@@ -306,7 +330,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     const int pos = prefix + t0 + tok;
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
     uint8_t *prow = smem + kOffP + hc * kHalf + r * 128;
-    float *red = reinterpret_cast<float *>(smem + kOffRed);  // [2 parity][2 half][128 rows]
+    // Exchange slots in TMEM columns 384 + 2 * parity + half (lane = row).
+    const uint32_t tX = tmem + 384 + lane_off;
     const float sl2 = p.scale_log2;
     const bool pos_scale = sl2 >= 0.f;
     float m = -INFINITY, l = 0.f;  // l: this half's share of the row sum
@@ -354,18 +379,36 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
       const float best = pos_scale ? fmaxf(fmaxf(r4[0], r4[1]), fmaxf(r4[2], r4[3]))
                                    : fminf(fminf(r4[0], r4[1]), fminf(r4[2], r4[3]));
       const float hmx = lim < 0 ? -INFINITY : best * sl2;  // this half's max, log2 domain
-      red[(s * 2 + hc) * 128 + r] = hmx;
+      tc::tmem_st1(tX + s * 2 + hc, hmx);
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
       if (softmax_pair_sync_any(bad)) {  // also publishes the halves' maxima
         ok = false;
         break;
       }
-      const float mx = fmaxf(hmx, red[(s * 2 + (hc ^ 1)) * 128 + r]);
+      tc::fence_after_sync();
+      const float other = tc::tmem_ld1(tX + s * 2 + (hc ^ 1));
+      tc::tmem_wait_ld();
+      const float mx = fmaxf(hmx, other);
       float m_new = m, alpha = 1.f;
       bool rescale = false;
       if (mx > m + 8.f) {
         m_new = mx;
         rescale = m != -INFINITY;
         alpha = rescale ? fast_exp2(m - m_new) : 0.f;
+      }
+      // Exponentials first (packed to 16-bit pairs in registers), while the
+      // tensor core may still be running P.V(j-1).
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      const float nb = m_new == -INFINITY ? 0.f : -m_new;  // masked: ex2(-inf) = 0
+      uint32_t pk[32];
+#pragma unroll
+      for (int c2 = 0; c2 < 32; ++c2) {
+        const float e0 = fast_exp2(fmaf(x[2 * c2], sl2, nb));
+        const float e1 = fast_exp2(fmaf(x[2 * c2 + 1], sl2, nb));
+        rs4[(2 * c2) & 3] += e0;
+        rs4[(2 * c2 + 1) & 3] += e1;
+        pk[c2] = pack2(e0, e1, kBf16);
       }
       // The single P buffer and O are free once P.V(j-1) is done.
       if (j >= 1) {
@@ -387,23 +430,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
           tc::tmem_wait_st();
         }
       }
-      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
-      const float nb = m_new == -INFINITY ? 0.f : -m_new;  // masked: ex2(-inf) = 0
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        float e[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          e[i] = fast_exp2(fmaf(x[c8 * 8 + i], sl2, nb));
-          rs4[i & 3] += e[i];
-        }
-        uint4 w;
-        w.x = pack2(e[0], e[1], kBf16);
-        w.y = pack2(e[2], e[3], kBf16);
-        w.z = pack2(e[4], e[5], kBf16);
-        w.w = pack2(e[6], e[7], kBf16);
-        *reinterpret_cast<uint4 *>(prow + ((c8 ^ (r & 7)) << 4)) = w;
-      }
+      for (int c8 = 0; c8 < 8; ++c8)
+        *reinterpret_cast<uint4 *>(prow + ((c8 ^ (r & 7)) << 4)) =
+            make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
       l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
       m = m_new;
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
@@ -412,12 +442,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
     }
     // Row sum of both halves; the barrier also settles a pending abort.
     if (ok) {
-      red[((nkv & 1) * 2 + hc) * 128 + r] = l;
+      tc::tmem_st1(tX + (nkv & 1) * 2 + hc, l);
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
       ok = !softmax_pair_sync_any(bad);
     }
     float L = 0.f;
     if (ok) {
-      L = l + red[((nkv & 1) * 2 + (hc ^ 1)) * 128 + r];
+      tc::fence_after_sync();
+      L = l + tc::tmem_ld1(tX + (nkv & 1) * 2 + (hc ^ 1));
+      tc::tmem_wait_ld();
       const int good = mbar_wait_bounded(&bar[B_ODONE + ((nkv - 1) & 1)], ((nkv - 1) >> 1) & 1, p.status);
       ok = __all_sync(0xffffffffu, good);
     }
