@@ -243,6 +243,73 @@ def measure_long_b1(device, reps: int = 20):
             "peak_source": f"hbm_gbs of {src}", "tok_per_s": round(1000.0 / ms, 1)}
 
 
+def measure_long_batch(device, layers: int = 36, pools: int = 4, reps: int = 3):
+    """BASELINE configs[4] run (a): 256 Qwen3-8B-shaped sequences, contexts
+    U[4096, 32768], 36 layers.
+
+    One layer's KV is ~19 GB, so the 36 layer launches cycle over `pools`
+    distinct layer pools (each far larger than L2) -- the per-GPU share of
+    the 8-GPU configuration.  Store + decode per layer, one CUDA graph.
+    """
+    import torch
+
+    import microinfer_b200 as mi
+    from oracle.paged_oracle import decode_bytes, store_bytes
+
+    n, hq, hkv = 256, 32, 8
+    g = torch.Generator(device="cpu").manual_seed(7)
+    ctx = torch.randint(4096, 32769, (n,), generator=g, dtype=torch.int32)
+    need = [(int(c) + BS - 1) // BS for c in ctx]
+    nb = sum(need) + 1
+    table = torch.full((n, max(need)), -1, dtype=torch.int32)
+    perm = torch.randperm(nb, generator=g).to(torch.int32)
+    at = 0
+    for r, k in enumerate(need):
+        table[r, :k] = perm[at:at + k]
+        at += k
+    pos = (ctx - 1).long()
+    slots = (table[torch.arange(n), pos // BS].long() * BS + pos % BS).to(torch.int32)
+    pool = mi.KVCache(pools, nb, BS, hkv, D, dtype=torch.bfloat16, device=device)
+    gd = torch.Generator(device=device).manual_seed(7)
+    pool.keys.normal_(generator=gd).mul_(0.5)
+    pool.values.normal_(generator=gd).mul_(0.5)
+    ctx_d, table_d, slots_d = ctx.to(device), table.to(device), slots.to(device)
+    q = torch.randn(layers, n, hq, D, generator=gd, device=device).to(torch.bfloat16)
+    kn = torch.randn(layers, n, hkv, D, generator=gd, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    kernel, split, _ = mi.decode_plan(n, hq, hkv, D, torch.bfloat16, BS, 0, device, table.shape[1])
+    views = [pool.layer(i) for i in range(pools)]
+
+    def run():
+        for i in range(layers):
+            v = views[i % pools]
+            mi.paged_decode_store(q[i], v.keys, v.values, table_d, ctx_d, kn[i], kn[i], slots_d,
+                                  split_k=split, out=out[i], early_kv=True)
+
+    run()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run()
+    graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / reps
+    b = layers * (decode_bytes(ctx.tolist(), hq, hkv, D, 2, BS) + store_bytes(n, hkv, D, 2))
+    del graph, pool
+    peaks, src = _peaks()
+    gbs = b / (ms * 1e-3) / 1e9
+    return {"workload": "BASELINE configs[4] run (a): 256 seqs, contexts U[4096,32768], 32q/8kv, "
+                        f"D128, 36 layers over {pools} distinct ~19 GB layer pools, bs16",
+            "kernel": kernel, "split_k": split, "ms_per_step": round(ms, 3),
+            "value": round(gbs, 1), "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
+            "peak_source": f"hbm_gbs of {src}", "tok_per_s": round(n * 1000.0 / ms, 1)}
+
+
 def _prefill_batch(workload: str, device, g):
     """Metadata + per-layer-shaped inputs for BASELINE configs[2] / configs[3]."""
     import torch
@@ -711,6 +778,7 @@ def run_ours(args):
         }
         if world == 1:
             line["extra"] = {"long_context_b1": measure_long_b1(device),
+                             "long_context_batch256": measure_long_batch(device),
                              "prefill_mixed": measure_prefill(device, "mixed"),
                              "prefill_shared_prefix": measure_prefill(device, "prefix")}
         if world == 1 and not args.no_cpu_baseline:

@@ -14,8 +14,8 @@
 // ring: per chunk one TMA copy per 64-dim half for K and for V (3-D tensor
 // map over [slots][Hkv][D], box {64, 1, 16}, 128-byte swizzle, so ldmatrix
 // reads are bank-conflict free).  Pages beyond the ring are prefetched into
-// L2 before the dependency wait (early_kv), the block table through a
-// sliding window.  Online softmax in the log2 domain with lazy rescale; the
+// L2 before the dependency wait (early_kv), the block table in batches of
+// 32 chunks loaded a batch ahead.  Online softmax in the log2 domain with lazy rescale; the
 // warps merge in shared memory, the splits through the workspace
 // (split_merge.cuh).  With the fused store, this step's token is folded in as
 // a one-key chunk built from k_new/v_new (by the warp with the fewest chunks,
@@ -155,9 +155,14 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     return col < p.bt_stride ? __ldg(table + col) : -1;
   };
   constexpr int kWin = kStagesM + kAheadM;
-  int32_t win[kWin];  // win[j]: page of chunk it + j of this warp's loop
-#pragma unroll
-  for (int j = 0; j < kWin; ++j) win[j] = table_entry(chunk_of(j));
+  // Pages in batches of 32 loop iterations: lane L holds the page of
+  // iteration 32 * batch + L; the next batch is loaded a whole batch ahead
+  // and page(it) is a shuffle, so no register move waits on a recent load.
+  int32_t pg_cur = table_entry(chunk_of(lane)), pg_nxt = table_entry(chunk_of(32 + lane));
+  auto page = [&](int it_now, int idx) -> int32_t {  // page of iteration idx (idx >= it_now)
+    const int32_t a = __shfl_sync(kAll, pg_cur, idx & 31), b = __shfl_sync(kAll, pg_nxt, idx & 31);
+    return (idx >> 5) == (it_now >> 5) ? a : b;
+  };
   int ctx = __ldg(p.context_lens + seq);
   const int64_t slot = fused ? static_cast<int64_t>(__ldg(p.slot_mapping + seq)) : -1;
   const int64_t cap = p.bt_stride * p.block_size;
@@ -212,13 +217,13 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
 #pragma unroll
   for (int s = 0; s < kStagesM; ++s) {
     if (s < my_n) {
-      issue(chunk_of(s), s, checked(win[s]));
+      issue(chunk_of(s), s, checked(page(0, s)));
       ++issued;
     }
   }
 #pragma unroll
   for (int j = kStagesM; j < kWin; ++j) {
-    const int32_t blk = win[j];
+    const int32_t blk = page(0, j);
     if (lane == 0 && j < my_n && blk >= 0 && blk < p.num_blocks) {
       const int row = row_of(chunk_of(j), blk);
 #pragma unroll
@@ -355,13 +360,14 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     process(kt, vt, valid);
     __syncwarp();  // every lane's ldmatrix of this stage is done before it is refilled
     if (it + kStagesM < my_n) {
-      issue(chunk_of(it + kStagesM), st, checked(win[kStagesM]));
+      issue(chunk_of(it + kStagesM), st, checked(page(it, it + kStagesM)));
       ++issued;
     }
     // Rolling L2 prefetch of the chunk kWin - 1 ahead (the prologue covered
     // the first kWin), so long contexts keep kWin chunks per warp in flight.
+    const int32_t pf_blk = page(it, it + kWin - 1);
     if (it > 0 && lane == 0 && it + kWin - 1 < my_n) {
-      const int32_t blk = win[kWin - 1];
+      const int32_t blk = pf_blk;
       if (blk >= 0 && blk < p.num_blocks) {
         const int row = row_of(chunk_of(it + kWin - 1), blk);
 #pragma unroll
@@ -371,9 +377,10 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
         }
       }
     }
-#pragma unroll
-    for (int j = 0; j < kWin - 1; ++j) win[j] = win[j + 1];
-    win[kWin - 1] = it + kWin < my_n ? table_entry(chunk_of(it + kWin)) : -1;
+    if ((it & 31) == 31) {  // the next iteration starts batch (it + 1) / 32
+      pg_cur = pg_nxt;
+      pg_nxt = table_entry(chunk_of(it + 33 + lane));
+    }
   }
   if (timed_out) {
     if (lane == 0)
