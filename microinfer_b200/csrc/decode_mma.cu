@@ -4,10 +4,11 @@
 // costs about the same time at N=16 as at N=256, so the swap-AB tcgen05
 // kernel spends ~1 us of tensor time per 128-key tile; CUDA-core dot
 // products cost ~26 warp instructions per key.  The warp-level m16n8k16 MMA
-// does a 16-key chunk of a kv head in 32 MMAs + 16 ldmatrix:
-//   S[16 x 16 keys]  = Q[16 x D] . K^T   (rows >= G of Q are zero)
-//   O[16 x D]       += P[16 x 16] . V      (P re-packed from S's registers)
-// i.e. ~5 warp instructions per key, with everything in registers.
+// does a 16-key chunk of a kv head in 16 MMAs + 17 ldmatrix, with the keys
+// in the M dimension and the GQA group in N = 8:
+//   S^T[16 keys x 8]  = K . Q^T            (columns >= G of Q^T are zero)
+//   O^T[D x 8]       += V^T . P^T          (P^T through 256 B of shared memory)
+// i.e. ~3 warp instructions per key, accumulators in registers.
 //
 // One CTA per (split, kv head, sequence), 8 warps.  Each warp streams its
 // own 16-key chunks (ids strided over splits and warps) through a 3-stage
@@ -55,11 +56,11 @@ struct MmaCfg {
   static constexpr int kTileBytes = kHalves * 2048;  // 16 rows x D of one operand
   static constexpr int kStageBytes = 2 * kTileBytes;
   static constexpr int kKSteps = D / 16;
-  static constexpr int kNBlocks = D / 8;
   static constexpr int kSmemStages = kWarpsM * kStagesM * kStageBytes;
   static constexpr int kSmemFold = kStageBytes;  // this step's token as a one-key chunk
+  static constexpr int kSmemPT = kWarpsM * 256;   // per warp: P^T of a chunk, [16 keys][8 queries]
   static constexpr int kSmemBars = kWarpsM * kStagesM * 8;
-  static constexpr int kSmem = kSmemStages + kSmemFold + kSmemBars + 16 + 1024;  // + alignment slack
+  static constexpr int kSmem = kSmemStages + kSmemFold + kSmemPT + kSmemBars + 16 + 1024;  // + slack
   static_assert(kWarpsM * 8 * (D + 2) * 4 <= kSmemStages, "merge buffers alias the ring");
 };
 
@@ -103,6 +104,32 @@ __device__ __forceinline__ void mma_rows8(float (&d)[4], uint32_t a0, uint32_t a
   }
 }
 
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t &r0, uint32_t &r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];"
+               : "=r"(r0), "=r"(r1)
+               : "r"(addr)
+               : "memory");
+}
+
+// d += A . B for m16n8k16 with fp32 accumulation, full A fragment.
+template <typename T>
+__device__ __forceinline__ void mma_full(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+  }
+}
+
 // Two floats -> one register of T pairs (lo in the low half).
 template <typename T>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
@@ -125,7 +152,8 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
   uint8_t *fold_tile = smem + C::kSmemStages;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kSmemStages + C::kSmemFold);
+  uint8_t *pt_smem = fold_tile + C::kSmemFold;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(pt_smem + C::kSmemPT);
   int *last_flag = reinterpret_cast<int *>(bars + kWarpsM * kStagesM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -238,8 +266,9 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     pdl_wait();
   }
 
-  // Query rows of the group as m16n8k16 A fragments: row g < G is query head
-  // kvh * G + g; a0 holds dims ks*16 + 2t, +1 and a2 dims ks*16 + 8 + 2t, +1.
+  // Q^T of the group as m16n8k16 B fragments (column n = query g of the
+  // group, zero for g >= G): b0 holds dims ks*16 + 2t, +1, b1 dims
+  // ks*16 + 8 + 2t, +1.
   uint32_t qa[C::kKSteps][2];
   {
     const T *qrow = static_cast<const T *>(p.query) +
@@ -251,11 +280,14 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     }
   }
   const float sl2 = p.scale_log2;
+  const uint32_t pbuf = smem_addr(pt_smem + warp * 256);
 
-  float o[C::kNBlocks][4];
+  // O^T accumulators: o[db] = O^T[dims db*16 + g, + 8][queries 2t, 2t + 1]
+  // as {(g, 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1)}; softmax state per query.
+  float o[D / 16][4];
 #pragma unroll
-  for (int nb = 0; nb < C::kNBlocks; ++nb) o[nb][0] = o[nb][1] = o[nb][2] = o[nb][3] = 0.f;
-  float m_run = -INFINITY, l_run = 0.f;  // row g; l_run covers this lane's columns
+  for (int db = 0; db < D / 16; ++db) o[db][0] = o[db][1] = o[db][2] = o[db][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};  // queries 2t, 2t+1
 
   // Zero V rows [valid, 16) of a chunk so P = 0 never meets stale values.
   auto zero_v_tail = [&](uint32_t vtile, int valid) {
@@ -266,55 +298,66 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     }
   };
 
-  // One chunk: S = Q K^T, online softmax, O += P V.
+  // One chunk, "swapped": S^T = K . Q^T (keys in M, the group in N = 8),
+  // online softmax per query column, O^T += V^T . P^T with P^T handed from
+  // the accumulator layout to the B-operand layout through 256 bytes of
+  // shared memory.  16 MMAs per 16-key chunk.
   auto process = [&](uint32_t ktile, uint32_t vtile, int valid) {
-    // two accumulator sets per key block (even / odd k-steps) halve the
-    // dependent MMA chain
-    float s0[2][4] = {}, s1[2][4] = {};
+    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};  // even / odd k-steps
     const int mi = lane >> 3, rr = lane & 7;
 #pragma unroll
     for (int ks = 0; ks < C::kKSteps; ++ks) {
-      uint32_t b00, b01, b10, b11;  // keys 0-7 / 8-15, dims lo / hi 8 of the k-step
-      ldsm_x4(swz(ktile, (mi >> 1) * 8 + rr, ks * 2 + (mi & 1)), b00, b01, b10, b11);
-      mma_rows8<T>(s0[ks & 1], qa[ks][0], qa[ks][1], b00, b01);
-      mma_rows8<T>(s1[ks & 1], qa[ks][0], qa[ks][1], b10, b11);
+      uint32_t a0, a1, a2, a3;  // (keys 0-7 | 8-15) x (dims lo 8 | hi 8 of the k-step)
+      ldsm_x4(swz(ktile, (mi & 1) * 8 + rr, ks * 2 + (mi >> 1)), a0, a1, a2, a3);
+      if (ks & 1)
+        mma_full<T>(sb, a0, a1, a2, a3, qa[ks][0], qa[ks][1]);
+      else
+        mma_full<T>(sa, a0, a1, a2, a3, qa[ks][0], qa[ks][1]);
     }
-    // row g, keys 2t, 2t+1, 8+2t, 9+2t
-    float x[4] = {s0[0][0] + s0[1][0], s0[0][1] + s0[1][1], s1[0][0] + s1[1][0],
-                  s1[0][1] + s1[1][1]};
-    const int kidx[4] = {2 * t, 2 * t + 1, 8 + 2 * t, 9 + 2 * t};
-    float mx = -INFINITY;
+    // x: (key g, query 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1)
+    const bool k0 = g < valid, k1 = g + 8 < valid;
+    float x[4] = {k0 ? (sa[0] + sb[0]) * sl2 : -INFINITY, k0 ? (sa[1] + sb[1]) * sl2 : -INFINITY,
+                  k1 ? (sa[2] + sb[2]) * sl2 : -INFINITY, k1 ? (sa[3] + sb[3]) * sl2 : -INFINITY};
+    float mx[2] = {fmaxf(x[0], x[2]), fmaxf(x[1], x[3])};
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      x[j] = kidx[j] < valid ? x[j] * sl2 : -INFINITY;
-      mx = fmaxf(mx, x[j]);
+    for (int off = 4; off < 32; off <<= 1) {
+      mx[0] = fmaxf(mx[0], __shfl_xor_sync(kAll, mx[0], off));
+      mx[1] = fmaxf(mx[1], __shfl_xor_sync(kAll, mx[1], off));
     }
-    mx = fmaxf(mx, __shfl_xor_sync(kAll, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(kAll, mx, 2));
-    if (mx > m_run + 8.f) {  // lazy rescale: the four lanes of a row agree
-      const float alpha = m_run == -INFINITY ? 0.f : fast_exp2(m_run - mx);
 #pragma unroll
-      for (int nb = 0; nb < C::kNBlocks; ++nb) {
-        o[nb][0] *= alpha;
-        o[nb][1] *= alpha;
+    for (int c = 0; c < 2; ++c) {
+      if (mx[c] > m_run[c] + 8.f) {  // lazy rescale: the lanes of a query column agree
+        const float alpha = m_run[c] == -INFINITY ? 0.f : fast_exp2(m_run[c] - mx[c]);
+#pragma unroll
+        for (int db = 0; db < D / 16; ++db) {
+          o[db][c] *= alpha;
+          o[db][c + 2] *= alpha;
+        }
+        l_run[c] *= alpha;
+        m_run[c] = mx[c];
       }
-      l_run *= alpha;
-      m_run = mx;
     }
     float pr[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      pr[j] = x[j] == -INFINITY ? 0.f : fast_exp2(x[j] - m_run);
-      l_run += pr[j];
-    }
-    const uint32_t pa0 = pack2<T>(pr[0], pr[1]), pa2 = pack2<T>(pr[2], pr[3]);
+    for (int j = 0; j < 4; ++j) pr[j] = x[j] == -INFINITY ? 0.f : fast_exp2(x[j] - m_run[j & 1]);
+    l_run[0] += pr[0] + pr[2];
+    l_run[1] += pr[1] + pr[3];
+    // P^T rows (keys) of 8 queries x 16 bits
+    asm volatile("st.shared.b32 [%0], %1;" ::"r"(pbuf + g * 16 + 4 * t), "r"(pack2<T>(pr[0], pr[1]))
+                 : "memory");
+    asm volatile("st.shared.b32 [%0], %1;" ::"r"(pbuf + (g + 8) * 16 + 4 * t),
+                 "r"(pack2<T>(pr[2], pr[3]))
+                 : "memory");
+    __syncwarp();
+    uint32_t pb0, pb1;
+    ldsm_x2_t(pbuf + (lane & 15) * 16, pb0, pb1);
 #pragma unroll
-    for (int np = 0; np < C::kNBlocks / 2; ++np) {
-      uint32_t v0, v1, v2, v3;  // (keys 0-7 | 8-15) x (dims np*16 + 0..7 | 8..15)
-      ldsm_x4_t(swz(vtile, (mi & 1) * 8 + rr, np * 2 + (mi >> 1)), v0, v1, v2, v3);
-      mma_rows8<T>(o[2 * np], pa0, pa2, v0, v1);
-      mma_rows8<T>(o[2 * np + 1], pa0, pa2, v2, v3);
+    for (int db = 0; db < D / 16; ++db) {
+      uint32_t a0, a1, a2, a3;  // V^T: (dims lo 8 | hi 8 of the block) x (keys 0-7 | 8-15)
+      ldsm_x4_t(swz(vtile, (mi >> 1) * 8 + rr, db * 2 + (mi & 1)), a0, a1, a2, a3);
+      mma_full<T>(o[db], a0, a1, a2, a3, pb0, pb1);
     }
+    __syncwarp();  // every lane has read P^T before the next chunk rewrites it
   };
 
   // ---- this step's token, as a one-key chunk in its own buffer, first ----
@@ -387,25 +430,32 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
       for (int it = consumed + 1; it < issued; ++it)
         if (!mbar_wait_bounded(&wbar[it % kStagesM], (it / kStagesM) & 1, p.status)) break;
     __syncwarp();
-    m_run = -INFINITY;
+    m_run[0] = m_run[1] = -INFINITY;
   }
 
   pdl_launch_dependents();
 
   // ---- merge the warps (shared memory aliases the drained ring) ----
-  l_run += __shfl_xor_sync(kAll, l_run, 1);
-  l_run += __shfl_xor_sync(kAll, l_run, 2);
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) l_run[c] += __shfl_xor_sync(kAll, l_run[c], off);
   __syncthreads();
   float *mg_acc = reinterpret_cast<float *>(smem);  // [warps][G][D]
   float *mg_ml = mg_acc + kWarpsM * G * D;          // [warps][G][2]
-  if (g < G) {
 #pragma unroll
-    for (int nb = 0; nb < C::kNBlocks; ++nb)
-      *reinterpret_cast<float2 *>(&mg_acc[(warp * G + g) * D + nb * 8 + 2 * t]) =
-          make_float2(o[nb][0], o[nb][1]);
-    if (t == 0) {
-      mg_ml[(warp * G + g) * 2] = m_run;
-      mg_ml[(warp * G + g) * 2 + 1] = l_run;
+  for (int c = 0; c < 2; ++c) {
+    const int q = 2 * t + c;
+    if (q < G) {
+#pragma unroll
+      for (int db = 0; db < D / 16; ++db) {
+        mg_acc[(warp * G + q) * D + db * 16 + g] = o[db][c];
+        mg_acc[(warp * G + q) * D + db * 16 + g + 8] = o[db][c + 2];
+      }
+      if (g == 0) {
+        mg_ml[(warp * G + q) * 2] = m_run[c];
+        mg_ml[(warp * G + q) * 2 + 1] = l_run[c];
+      }
     }
   }
   __syncthreads();
