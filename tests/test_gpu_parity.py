@@ -457,3 +457,46 @@ def test_bounded_wait_times_out_and_context_survives(cuda_device):
               _lib.stream_of(cuda_device))
     assert _lib.read_device_status(cuda_device) == 0
     assert (torch.ones(4, device="cuda") * 2).sum().item() == 8
+
+
+# --- warp-level MMA decode over the shapes the golden cases do not reach ----
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("d,g", [(64, 1), (64, 8), (128, 4), (128, 8)])
+@pytest.mark.parametrize("bs,split", [(16, 1), (32, 3), (64, 0)])
+@pytest.mark.parametrize("fused", [False, True])
+def test_mma_decode_shapes_match_oracle(dtype, d, g, bs, split, fused):
+    torch_dt = TORCH[dtype]
+    n, hkv, nb = 3, 2, 48
+    hq = hkv * g
+    gen = torch.Generator().manual_seed(d * 100 + g * 10 + bs)
+    ctx = torch.randint(1, nb * bs // n, (n,), generator=gen, dtype=torch.int32)
+    width = (int(ctx.max()) + bs - 1) // bs
+    table = torch.full((n, width), -1, dtype=torch.int32)
+    perm = torch.randperm(nb, generator=gen).to(torch.int32)
+    at = 0
+    for r in range(n):
+        k = (int(ctx[r]) + bs - 1) // bs
+        table[r, :k] = perm[at:at + k]
+        at += k
+    kernel, _, _ = mi.decode_plan(n, hq, hkv, d, torch_dt, bs, split, "cuda", width)
+    if "MICROINFER_B200_DECODE" not in os.environ:
+        assert kernel == "mma"
+    kc = (torch.randn(nb, bs, hkv, d, generator=gen) * 0.5).to(torch_dt).cuda()
+    vc = (torch.randn(nb, bs, hkv, d, generator=gen) * 0.5).to(torch_dt).cuda()
+    q = torch.randn(n, hq, d, generator=gen).to(torch_dt).cuda()
+    table_d, ctx_d = table.cuda(), ctx.cuda()
+    scale = 1.0 / math.sqrt(d)
+    if fused:
+        kn = (torch.randn(n, hkv, d, generator=gen) * 0.5).to(torch_dt).cuda()
+        vn = (torch.randn(n, hkv, d, generator=gen) * 0.5).to(torch_dt).cuda()
+        pos = (ctx - 1).long()
+        slots = (table[torch.arange(n), pos // bs].long() * bs + pos % bs).to(torch.int32).cuda()
+        out = mi.paged_decode_store(q, kc, vc, table_d, ctx_d, kn, vn, slots, scale=scale,
+                                    split_k=split or None, early_kv=True)
+    else:
+        out = mi.paged_decode(q, kc, vc, table_d, ctx_d, scale=scale, split_k=split or None)
+    torch.cuda.synchronize()
+    expected = po.paged_decode(host(q, dtype), host(kc, dtype), host(vc, dtype), table.numpy(),
+                               ctx.numpy(), scale=scale, dtype=dtype)
+    assert_close(out, expected, dtype)
