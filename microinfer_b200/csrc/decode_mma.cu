@@ -16,11 +16,12 @@
 // map over [slots][Hkv][D], box {64, 1, 16}, 128-byte swizzle, so ldmatrix
 // reads are bank-conflict free).  Pages beyond the ring are prefetched into
 // L2 before the dependency wait (early_kv), the block table in batches of
-// 32 chunks loaded a batch ahead.  Online softmax in the log2 domain with lazy rescale; the
-// warps merge in shared memory, the splits through the workspace
-// (split_merge.cuh).  With the fused store, this step's token is folded in as
-// a one-key chunk built from k_new/v_new (by the warp with the fewest chunks,
-// right after the dependency wait) and written to its slot.
+// 32 chunks loaded a batch ahead.  Online softmax in the log2 domain with
+// lazy rescale; the warps merge in shared memory, the splits through the
+// workspace (split_merge.cuh).  With the fused store, this step's token is
+// folded in as a one-key chunk built from k_new/v_new (the last item of the
+// warp with the fewest chunks, in one of its free ring stages, so the load of
+// k_new/v_new hides behind the cached chunks) and written to its slot.
 //
 // V rows past the context in a partial chunk are zeroed before P.V, so stale
 // pool contents (even non-finite) never reach the output.  Every wait is
@@ -57,10 +58,9 @@ struct MmaCfg {
   static constexpr int kStageBytes = 2 * kTileBytes;
   static constexpr int kKSteps = D / 16;
   static constexpr int kSmemStages = kWarpsM * kStagesM * kStageBytes;
-  static constexpr int kSmemFold = kStageBytes;  // this step's token as a one-key chunk
   static constexpr int kSmemPT = kWarpsM * 256;   // per warp: P^T of a chunk, [16 keys][8 queries]
   static constexpr int kSmemBars = kWarpsM * kStagesM * 8;
-  static constexpr int kSmem = kSmemStages + kSmemFold + kSmemPT + kSmemBars + 16 + 1024;  // + slack
+  static constexpr int kSmem = kSmemStages + kSmemPT + kSmemBars + 16 + 1024;  // + slack
   static_assert(kWarpsM * 8 * (D + 2) * 4 <= kSmemStages, "merge buffers alias the ring");
 };
 
@@ -151,16 +151,13 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
-  uint8_t *fold_tile = smem + C::kSmemStages;
-  uint8_t *pt_smem = fold_tile + C::kSmemFold;
+  uint8_t *pt_smem = smem + C::kSmemStages;
   uint64_t *bars = reinterpret_cast<uint64_t *>(pt_smem + C::kSmemPT);
   int *last_flag = reinterpret_cast<int *>(bars + kWarpsM * kStagesM);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;  // fragment row / column pair
-  const int split = blockIdx.x, nsplit = gridDim.x;
   const int kvh = blockIdx.y;
-  const int64_t seq = blockIdx.z;
   uint64_t *wbar = bars + warp * kStagesM;
   uint8_t *wstage = smem + warp * kStagesM * C::kStageBytes;
   const bool fused = p.k_new != nullptr;
@@ -176,6 +173,9 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
 
   // Without early_kv everything below may come from the preceding kernel.
   if (!p.early_kv) pdl_wait();
+
+  const int split = blockIdx.x, nsplit = gridDim.x;
+  const int64_t seq = blockIdx.z;
   const int32_t *table = p.block_tables + seq * p.bt_stride;
   auto chunk_of = [&](int it) { return split + nsplit * (warp + kWarpsM * it); };
   auto table_entry = [&](int ci) -> int32_t {  // page of chunk ci (block_size % 16 == 0)
@@ -298,13 +298,30 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     }
   };
 
-  // One chunk, "swapped": S^T = K . Q^T (keys in M, the group in N = 8),
-  // online softmax per query column, O^T += V^T . P^T with P^T handed from
-  // the accumulator layout to the B-operand layout through 256 bytes of
-  // shared memory.  16 MMAs per 16-key chunk.
+  // This step's token (fused store) is the owning warp's last item: its K/V
+  // rows are loaded here and written to shared memory and to their slot only
+  // when that item comes up, so the load latency hides behind the cached
+  // chunks.  Its one-key chunk sits in ring stage my_n % kStagesM, which holds
+  // no chunk still to be processed by then (no refill reaches chunk my_n).
+  const uint32_t fold_k = smem_addr(wstage + (my_n % kStagesM) * C::kStageBytes);
+  const uint32_t fold_v = fold_k + C::kTileBytes;
+  const bool new_lane = own_new && lane < 2 * (D / 8);
+  const int new_kind = lane / (D / 8), new_cj = lane % (D / 8);
+  uint4 new_row = make_uint4(0u, 0u, 0u, 0u);
+  if (new_lane) {
+    const int64_t off = seq * p.new_token_stride_bytes + static_cast<int64_t>(kvh) * D * sizeof(T);
+    new_row = *reinterpret_cast<const uint4 *>((new_kind ? p.v_new : p.k_new) + off + new_cj * 16);
+  }
+  const int n_items = my_n + (own_new ? 1 : 0);
+
+  // One chunk in the "swapped" form: S^T = K . Q^T (keys in M, the group in
+  // N = 8), online softmax per query column, O^T += V^T . P^T with P^T handed
+  // from the accumulator layout to the B-operand layout through 256 bytes of
+  // shared memory.  16 MMAs per 16-key chunk.  The V^T fragments are loaded
+  // right after the S MMAs so their latency overlaps the softmax.
   auto process = [&](uint32_t ktile, uint32_t vtile, int valid) {
-    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};  // even / odd k-steps
     const int mi = lane >> 3, rr = lane & 7;
+    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};  // even / odd k-steps
 #pragma unroll
     for (int ks = 0; ks < C::kKSteps; ++ks) {
       uint32_t a0, a1, a2, a3;  // (keys 0-7 | 8-15) x (dims lo 8 | hi 8 of the k-step)
@@ -314,6 +331,11 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
       else
         mma_full<T>(sa, a0, a1, a2, a3, qa[ks][0], qa[ks][1]);
     }
+    uint32_t va[D / 16][4];  // V^T: (dims lo 8 | hi 8 of the block) x (keys 0-7 | 8-15)
+#pragma unroll
+    for (int db = 0; db < D / 16; ++db)
+      ldsm_x4_t(swz(vtile, (mi >> 1) * 8 + rr, db * 2 + (mi & 1)), va[db][0], va[db][1], va[db][2],
+                va[db][3]);
     // x: (key g, query 2t), (g, 2t+1), (g+8, 2t), (g+8, 2t+1)
     const bool k0 = g < valid, k1 = g + 8 < valid;
     float x[4] = {k0 ? (sa[0] + sb[0]) * sl2 : -INFINITY, k0 ? (sa[1] + sb[1]) * sl2 : -INFINITY,
@@ -352,66 +374,59 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     uint32_t pb0, pb1;
     ldsm_x2_t(pbuf + (lane & 15) * 16, pb0, pb1);
 #pragma unroll
-    for (int db = 0; db < D / 16; ++db) {
-      uint32_t a0, a1, a2, a3;  // V^T: (dims lo 8 | hi 8 of the block) x (keys 0-7 | 8-15)
-      ldsm_x4_t(swz(vtile, (mi >> 1) * 8 + rr, db * 2 + (mi & 1)), a0, a1, a2, a3);
-      mma_full<T>(o[db], a0, a1, a2, a3, pb0, pb1);
-    }
-    __syncwarp();  // every lane has read P^T before the next chunk rewrites it
+    for (int db = 0; db < D / 16; ++db)
+      mma_full<T>(o[db], va[db][0], va[db][1], va[db][2], va[db][3], pb0, pb1);
+    __syncwarp();  // every lane has read P^T before the next item rewrites it
   };
 
-  // ---- this step's token, as a one-key chunk in its own buffer, first ----
-  if (own_new) {
-    const uint32_t kt = smem_addr(fold_tile), vt = kt + C::kTileBytes;
-    zero_v_tail(vt, 1);
-    const int64_t off = seq * p.new_token_stride_bytes + static_cast<int64_t>(kvh) * D * sizeof(T);
-    const bool store = slot < p.num_blocks * p.block_size;
-    if (lane < 2 * (D / 8)) {
-      const int kind = lane / (D / 8), cj = lane % (D / 8);
-      const uint4 v = *reinterpret_cast<const uint4 *>((kind ? p.v_new : p.k_new) + off + cj * 16);
-      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(swz(kind ? vt : kt, 0, cj)),
-                   "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
-                   : "memory");
-      if (store)
-        *reinterpret_cast<uint4 *>(const_cast<char *>(kind ? p.value_cache : p.key_cache) +
-                                   (slot * p.num_kv_heads + kvh) * D * sizeof(T) + cj * 16) = v;
-    }
-    if (!store && lane == 0) flag_status(p.status, MI_DEV_BAD_SLOT);
-    __syncwarp();
-    process(kt, vt, 1);
-  }
-
   bool timed_out = false;
-  int consumed = 0;
+  int consumed = 0;  // cached chunks whose copies have landed, in order
 #pragma unroll 1
-  for (int it = 0; it < my_n; ++it) {
-    const int st = it % kStagesM;
-    const int ci = chunk_of(it);
-    if (!mbar_wait_bounded(&wbar[st], (it / kStagesM) & 1, p.status)) {
-      timed_out = true;
-      break;
+  for (int it = 0; it < n_items; ++it) {
+    uint32_t kt, vt;
+    int valid;
+    if (it < my_n) {
+      const int st = it % kStagesM;
+      if (!mbar_wait_bounded(&wbar[st], (it / kStagesM) & 1, p.status)) {
+        timed_out = true;
+        break;
+      }
+      consumed = it + 1;
+      kt = smem_addr(wstage + st * C::kStageBytes);
+      vt = kt + C::kTileBytes;
+      valid = min(kChunk, ctx_kv - chunk_of(it) * kChunk);
+      if (valid < kChunk) {
+        zero_v_tail(vt, valid);
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      }
+    } else {  // this step's token, as a one-key chunk
+      kt = fold_k;
+      vt = fold_v;
+      valid = 1;
+      zero_v_tail(fold_v, 1);
+      if (new_lane) {
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(
+                         swz(new_kind ? fold_v : fold_k, 0, new_cj)),
+                     "r"(new_row.x), "r"(new_row.y), "r"(new_row.z), "r"(new_row.w)
+                     : "memory");
+        if (slot < p.num_blocks * p.block_size)
+          *reinterpret_cast<uint4 *>(const_cast<char *>(new_kind ? p.value_cache : p.key_cache) +
+                                     (slot * p.num_kv_heads + kvh) * D * sizeof(T) + new_cj * 16) =
+              new_row;
+      }
+      if (lane == 0 && slot >= p.num_blocks * p.block_size) flag_status(p.status, MI_DEV_BAD_SLOT);
     }
-    consumed = it + 1;
-    const uint32_t kt = smem_addr(wstage + st * C::kStageBytes);
-    const uint32_t vt = kt + C::kTileBytes;
-    const int valid = min(kChunk, ctx_kv - ci * kChunk);
-    if (valid < kChunk) {
-      zero_v_tail(vt, valid);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-    }
+    __syncwarp();  // zeroed rows and the token's row are visible to every lane
     process(kt, vt, valid);
-    __syncwarp();  // every lane's ldmatrix of this stage is done before it is refilled
-    if (it + kStagesM < my_n) {
-      issue(chunk_of(it + kStagesM), st, checked(page(it, it + kStagesM)));
-      ++issued;
-    }
-    // Rolling L2 prefetch of the chunk kWin - 1 ahead (the prologue covered
-    // the first kWin), so long contexts keep kWin chunks per warp in flight.
-    const int32_t pf_blk = page(it, it + kWin - 1);
-    if (it > 0 && lane == 0 && it + kWin - 1 < my_n) {
-      const int32_t blk = pf_blk;
-      if (blk >= 0 && blk < p.num_blocks) {
+    if (it < my_n) {
+      // Refill the stage just consumed, and keep the rolling L2 prefetch
+      // kWin - 1 chunks ahead (the prologue covered the first kWin).
+      if (it + kStagesM < my_n) {
+        issue(chunk_of(it + kStagesM), it % kStagesM, checked(page(it, it + kStagesM)));
+        ++issued;
+      }
+      const int32_t blk = page(it, it + kWin - 1);
+      if (it > 0 && lane == 0 && it + kWin - 1 < my_n && blk >= 0 && blk < p.num_blocks) {
         const int row = row_of(chunk_of(it + kWin - 1), blk);
 #pragma unroll
         for (int h = 0; h < C::kHalves; ++h) {
@@ -435,11 +450,12 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
 
   pdl_launch_dependents();
 
-  // ---- merge the warps (shared memory aliases the drained ring) ----
 #pragma unroll
   for (int c = 0; c < 2; ++c)
 #pragma unroll
     for (int off = 4; off < 32; off <<= 1) l_run[c] += __shfl_xor_sync(kAll, l_run[c], off);
+
+  // ---- merge the warps (shared memory aliases the drained ring) ----
   __syncthreads();
   float *mg_acc = reinterpret_cast<float *>(smem);  // [warps][G][D]
   float *mg_ml = mg_acc + kWarpsM * G * D;          // [warps][G][2]
