@@ -82,6 +82,14 @@ __device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
   return *reinterpret_cast<float2 *>(&rd);
 }
 
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  unsigned long long ra = *reinterpret_cast<unsigned long long *>(&a);
+  unsigned long long rb = *reinterpret_cast<unsigned long long *>(&b);
+  unsigned long long rd;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
+  return *reinterpret_cast<float2 *>(&rd);
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -152,6 +160,36 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
 #pragma unroll 1
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t now = global_ns();
+    if (start == 0) {
+      start = now;
+    } else if (now - start > kWaitLimitNs) {
+      flag_status(status, MI_DEV_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// Non-suspending probe of a phase (mbarrier.test_wait).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// As mbar_wait_bounded, but spinning on test_wait so the caller sees the
+// phase flip at once instead of after a suspension; for a lone thread with
+// nothing else to do (an MMA issuer), never for whole warpgroups.
+__device__ __forceinline__ bool mbar_spin_bounded(uint64_t *bar, uint32_t parity, int32_t *status) {
+  uint64_t start = 0;
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 256; ++i)
+      if (mbar_test_wait(bar, parity)) return true;
     const uint64_t now = global_ns();
     if (start == 0) {
       start = now;

@@ -38,6 +38,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -491,6 +493,388 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   }
 }
 
+// ---------------------------------------------------------------------------
+// Two query tiles per CTA (prefill_tc2_kernel).
+//
+// CTA = (tile pair, kv head, sequence): query tiles A (tokens t0 .. t0+TQ-1)
+// and B (the next TQ tokens) of one kv head share every K/V tile, so each key
+// tile crosses into the SM once for 256 query rows.  352 threads:
+//   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B: one TMEM lane
+//               (= query row) per thread, the whole 128-key row in registers
+//   warp 8      TMA: Q of both tiles, then the K tiles (3-stage ring)
+//   warp 9      TMEM owner and single-thread MMA issuer
+//   warp 10     TMA: the V tiles (2-stage ring)
+// TMEM (512 columns): S_A at 0, S_B at 128, O_A at 256, O_B at 384.  The
+// softmax writes P (16-bit pairs) over the first 64 columns of its S and P.V
+// reads A from TMEM, so P never goes through shared memory.  The MMA issuer
+// alternates the tiles,
+//   S_A(0) S_B(0) | PV_A(0) S_A(1) | PV_B(0) S_B(1) | PV_A(1) S_A(2) | ...
+// so one tile's softmax runs while the tensor core works for the other.
+// tcgen05.mma ops of one thread run in issue order: S_X(j+1) overwrites P_X(j)
+// only after PV_X(j) has read it, and once S_X(j+1) is complete PV_X(j) is
+// too, so the softmax may rescale O_X right after S_X(j+1) is ready.
+namespace {
+
+constexpr int kThreads2 = 352;
+constexpr int kOffQ2 = 0;  // Q_A, Q_B
+constexpr int kOffK2 = kOffQ2 + 2 * kTileBytes;
+constexpr int kOffV2 = kOffK2 + kKStages * kTileBytes;
+constexpr int kOffBar2 = kOffV2 + kVStages * kTileBytes;
+constexpr int kSmemBytes2 = kOffBar2 + 256 + 1024;
+
+enum {
+  C_Q = 0,
+  C_KFULL = 1,   // +K stage (3)
+  C_KEMPTY = 4,  // +K stage
+  C_VFULL = 7,   // +V stage (2)
+  C_VEMPTY = 9,  // +V stage
+  C_SFULL = 11,  // +tile: S_X(j) (and everything issued before it) done
+  C_PFULL = 13,  // +tile: P_X(j) in TMEM (128 softmax threads)
+  C_ODONE = 15,  // every MMA done
+  C_FIN = 16,
+  C_COUNT = 17
+};
+
+// Warp-uniform: this lane's wait succeeded in every lane and nobody aborted.
+__device__ __forceinline__ bool warp_all_ok(bool ok, const int *abort_flag) {
+  return __all_sync(0xffffffffu, ok && !*(volatile const int *)abort_flag);
+}
+
+}  // namespace
+
+template <typename T, int G>
+__global__ void __launch_bounds__(kThreads2, 1)
+    prefill_tc2_kernel(const __grid_constant__ PrefillTcParams p) {
+  constexpr int TQ = 128 / G;  // tokens per tile
+  constexpr bool kBf16 = sizeof(T) == 2 && Elem<T>::kDtype == MI_DTYPE_BFLOAT16;
+  constexpr uint32_t kIdescQK = tc::idesc_f16(128, 128, kBf16 ? 1 : 0, false);
+  constexpr uint32_t kIdescPV = tc::idesc_f16(128, 128, kBf16 ? 1 : 0, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kOffBar2);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + C_COUNT);
+  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
+  const uint32_t sQ = smem_addr(smem + kOffQ2);
+  const uint32_t sK = smem_addr(smem + kOffK2);
+  const uint32_t sV = smem_addr(smem + kOffV2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.y;
+  const int64_t seq = blockIdx.z;
+
+  pdl_wait();
+  const int q_start = p.cu_q[seq];
+  const int q_len = p.cu_q[seq + 1] - q_start;
+  const int t0 = blockIdx.x * 2 * TQ;
+  if (t0 >= q_len) return;  // uniform: this sequence has fewer tile pairs
+  const int kv0 = p.cu_k[seq];
+  const int ctx = p.cu_k[seq + 1] - kv0;
+  const int prefix = ctx - q_len;
+  const int nt[2] = {min(TQ, q_len - t0), max(0, min(TQ, q_len - t0 - TQ))};
+  int nkv_t[2];
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const int maxpos = prefix + t0 + x * TQ + nt[x] - 1;
+    nkv_t[x] = nt[x] > 0 && maxpos >= 0 ? maxpos / 128 + 1 : 0;
+  }
+  const int nkv = max(nkv_t[0], nkv_t[1]);
+  T *out = static_cast<T *>(p.out);
+  if (nkv == 0) {  // no visible key (context shorter than the chunk): zeros, as the generic kernel
+    for (int i = threadIdx.x; i < (nt[0] + nt[1]) * G * 128; i += kThreads2) {
+      const int row = i / 128, d = i % 128;
+      out[(static_cast<int64_t>(q_start + t0 + row / G) * p.num_q_heads + kvh * G + row % G) * 128 + d] =
+          Elem<T>::from_float(0.f);
+    }
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(&bar[C_Q], 1);
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(&bar[C_KFULL + s], 1);
+      mbar_init(&bar[C_KEMPTY + s], 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(&bar[C_VFULL + s], 1);
+      mbar_init(&bar[C_VEMPTY + s], 1);
+    }
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bar[C_SFULL + x], 1);
+      mbar_init(&bar[C_PFULL + x], 128);
+    }
+    mbar_init(&bar[C_ODONE], 1);
+    mbar_init(&bar[C_FIN], 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) tc::tmem_alloc(tmem_slot, kTmemCols);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8 || warp == 10) {
+    // ---------------------------------------------------------- producers
+    // warp 8 loads Q and the K tiles, warp 10 the V tiles.  Table lookups as in
+    // prefill_tc_kernel: batches of 4 tiles, one batch ahead.
+    const bool is_v = warp == 10;
+    const int32_t *table = p.block_tables + seq * p.bt_stride;
+    auto kv_entry = [&](int key0) -> int {
+      if (key0 >= ctx || !p.paged) return 0;
+      const int64_t col = key0 / p.block_size;
+      return col < p.bt_stride ? __ldg(table + col) : -1;
+    };
+    auto kv_row = [&](int key0, int entry) -> int {
+      if (key0 >= ctx) return static_cast<int>(p.kv_rows);  // past the context: zero fill
+      if (!p.paged) return kv0 + key0;
+      if (entry < 0 || entry >= p.num_blocks) {
+        flag_status(p.status, MI_DEV_BAD_BLOCK);
+        return static_cast<int>(p.kv_rows);
+      }
+      return static_cast<int>(static_cast<int64_t>(entry) * p.block_size + key0 % p.block_size);
+    };
+    bool ok = true;
+    int armed = 0;
+    if (lane == 0) {
+      tc::prefetch_tmap(is_v ? &p.tmap_v : &p.tmap_k);
+      if (!is_v) {
+        tc::prefetch_tmap(&p.tmap_q);
+        const int ntiles = nt[1] > 0 ? 2 : 1;
+        mbar_arrive_expect_tx(&bar[C_Q], ntiles * 2 * kHalf);
+        for (int x = 0; x < ntiles; ++x)
+          for (int dh = 0; dh < 2; ++dh)
+            tc::tma_load_3d(smem + kOffQ2 + x * kTileBytes + dh * kHalf, &p.tmap_q, dh * 64, kvh * G,
+                            q_start + t0 + x * TQ, &bar[C_Q]);
+      }
+    }
+    const int g = lane >> 1, dh = lane & 1;
+    const int nst = is_v ? kVStages : kKStages;
+    const CUtensorMap *map = is_v ? &p.tmap_v : &p.tmap_k;
+    uint8_t *ring = smem + (is_v ? kOffV2 : kOffK2);
+    const int full0 = is_v ? C_VFULL : C_KFULL, empty0 = is_v ? C_VEMPTY : C_KEMPTY;
+    const int bt = lane >> 3, bg = lane & 7;
+    auto entry_for = [&](int tile) { return tile < nkv ? kv_entry(tile * 128 + bg * 16) : 0; };
+    int cur = entry_for(bt), nxt = entry_for(4 + bt);
+    for (int j = 0; j < nkv && ok; ++j) {
+      const int s = j % nst;
+      const uint32_t empty_parity = ((j / nst) & 1) ^ 1;
+      if (j > 0 && (j & 3) == 0) {
+        cur = nxt;
+        nxt = entry_for(j + 4 + bt);
+      }
+      const int entry = __shfl_sync(0xffffffffu, cur, ((j & 3) * 8 + g) & 31);
+      const int row = lane < 16 ? kv_row(j * 128 + g * 16, entry) : 0;
+      int good = 1;
+      if (lane == 0)
+        good = mbar_wait_bounded(&bar[empty0 + s], empty_parity, p.status) && !*(volatile int *)abort_flag;
+      good = __shfl_sync(0xffffffffu, good, 0);
+      if (!good) {
+        ok = false;
+        break;
+      }
+      if (lane == 0) mbar_arrive_expect_tx(&bar[full0 + s], kTileBytes);
+      __syncwarp();
+      if (lane < 16)
+        tc::tma_load_3d(ring + s * kTileBytes + dh * kHalf + g * 2048, map, dh * 64, kvh, row, &bar[full0 + s]);
+      armed = j + 1;
+    }
+    if (!ok && lane == 0) {
+      *(volatile int *)abort_flag = 1;
+      // Let this CTA's own loads in flight land before its shared memory goes away.
+      for (int j = max(0, armed - nst); j < armed; ++j)
+        mbar_wait_bounded(&bar[full0 + j % nst], (j / nst) & 1, p.status);
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      auto s_mma = [&](int x, int j) {  // S_X(j) = Q_X K_j^T
+        const int ks = j % kKStages;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc::umma_f16(tmem + x * 128, kmajor_desc(sQ + x * kTileBytes, kk),
+                       kmajor_desc(sK + ks * kTileBytes, kk), kIdescQK, kk > 0 ? 1u : 0u);
+        tc::umma_commit(&bar[C_SFULL + x]);
+      };
+      auto pv_mma = [&](int x, int j) -> bool {  // O_X += P_X(j) V_j, P from TMEM
+        if (!mbar_spin_bounded(&bar[C_PFULL + x], j & 1, p.status)) return false;
+        tc::fence_after_sync();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc::umma_f16_tmem_a(tmem + 256 + x * 128, tmem + x * 128 + kk * 8,
+                              mnmajor_desc(sV + (j % kVStages) * kTileBytes, kk), kIdescPV,
+                              (j > 0 || kk > 0) ? 1u : 0u);
+        return true;
+      };
+      bool ok = mbar_spin_bounded(&bar[C_Q], 0, p.status) &&
+                mbar_spin_bounded(&bar[C_KFULL], 0, p.status) && !*(volatile int *)abort_flag;
+      if (ok) {
+        tc::fence_after_sync();
+        if (nkv_t[0] > 0) s_mma(0, 0);
+        if (nkv_t[1] > 0) s_mma(1, 0);
+        tc::umma_commit(&bar[C_KEMPTY]);
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        const bool nA = j + 1 < nkv_t[0], nB = j + 1 < nkv_t[1];
+        const int vs = j % kVStages, ks = (j + 1) % kKStages;
+        ok = mbar_spin_bounded(&bar[C_VFULL + vs], (j / kVStages) & 1, p.status) &&
+             (!(nA || nB) || mbar_spin_bounded(&bar[C_KFULL + ks], ((j + 1) / kKStages) & 1, p.status)) &&
+             !*(volatile int *)abort_flag;
+        if (!ok) break;
+        tc::fence_after_sync();
+        if (j < nkv_t[0] && !(ok = pv_mma(0, j))) break;
+        if (nA) s_mma(0, j + 1);
+        if (j < nkv_t[1] && !(ok = pv_mma(1, j))) break;
+        if (nB) s_mma(1, j + 1);
+        if (nA || nB) tc::umma_commit(&bar[C_KEMPTY + ks]);
+        tc::umma_commit(&bar[C_VEMPTY + vs]);
+      }
+      if (!ok) *(volatile int *)abort_flag = 1;
+      // Every MMA issued by this thread completes before the epilogue reads O
+      // and before TMEM is released.
+      tc::umma_commit(&bar[C_ODONE]);
+      tc::umma_commit(&bar[C_FIN]);
+      mbar_spin_bounded(&bar[C_FIN], 0, p.status);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int x = warp >= 4 ? 1 : 0;  // query tile
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;  // TMEM lane = query row of the tile
+    const int tok = r / G;
+    const bool rvalid = tok < nt[x];
+    const int pos = prefix + t0 + x * TQ + tok;
+    const int my_nkv = nkv_t[x];
+    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
+    const uint32_t tS = tmem + x * 128 + lane_off, tO = tmem + 256 + x * 128 + lane_off;
+    const float sl2 = p.scale_log2;
+    const bool pos_scale = sl2 >= 0.f;
+    const float masked = pos_scale ? -INFINITY : INFINITY;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < my_nkv; ++j) {
+      if (!warp_all_ok(mbar_wait_bounded(&bar[C_SFULL + x], j & 1, p.status), abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc::fence_after_sync();
+      // The whole row in registers: one TMEM round trip per tile.
+      float sr[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+        tc::tmem_ld32(tS + c * 32, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sr[c * 32 + i] = v[i];
+      }
+      tc::tmem_wait_ld();
+      // key c of the tile is visible iff c <= pos - j * 128: only diagonal
+      // tiles (and rows past the chunk) mask anything.
+      const int lim = rvalid ? pos - j * 128 : -1;
+      if (lim < 127) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) sr[c] = c <= lim ? sr[c] : masked;
+      }
+      float r4[4] = {masked, masked, masked, masked};
+      if (pos_scale) {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) r4[c & 3] = fmaxf(r4[c & 3], sr[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 128; ++c) r4[c & 3] = fminf(r4[c & 3], sr[c]);
+      }
+      const float best = pos_scale ? fmaxf(fmaxf(r4[0], r4[1]), fmaxf(r4[2], r4[3]))
+                                   : fminf(fminf(r4[0], r4[1]), fminf(r4[2], r4[3]));
+      const float mx = lim < 0 ? -INFINITY : best * sl2;  // row max, log2 domain
+      float m_new = m, alpha = 1.f;
+      bool rescale = false;
+      if (mx > m + 8.f) {
+        m_new = mx;
+        rescale = m != -INFINITY;
+        alpha = rescale ? fast_exp2(m - m_new) : 0.f;
+      }
+      // P = 2^(s * scale - m) as 16-bit pairs over the first 64 columns of S
+      // (the row is already read back).
+      const float nb = m_new == -INFINITY ? 0.f : -m_new;  // masked: ex2(-inf) = 0
+      const float2 sc2 = make_float2(sl2, sl2), nb2 = make_float2(nb, nb);
+      float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {  // keys 16q .. 16q+15 -> columns 8q .. 8q+7
+        float pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float2 a2 = ffma2(make_float2(sr[q * 16 + 2 * i], sr[q * 16 + 2 * i + 1]), sc2, nb2);
+          const float2 e = make_float2(fast_exp2(a2.x), fast_exp2(a2.y));
+          sum2[i & 1] = fadd2(sum2[i & 1], e);
+          pk[i] = __uint_as_float(pack2(e.x, e.y, kBf16));
+        }
+        tc::tmem_st8(tS + q * 8, pk);
+      }
+      // O_X is quiescent here (PV_X(j-1) completed before S_X(j) did) and
+      // PV_X(j) waits for this thread's arrival below.
+      if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
+        const float ra = rescale ? alpha : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          tc::tmem_ld32(tO + c * 32, o);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= ra;
+          tc::tmem_st32(tO + c * 32, o);
+        }
+      }
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(&bar[C_PFULL + x]);
+      const float2 s01 = fadd2(sum2[0], sum2[1]);
+      l = l * alpha + (s01.x + s01.y);
+      m = m_new;
+    }
+    if (ok && my_nkv > 0)
+      ok = warp_all_ok(mbar_wait_bounded(&bar[C_ODONE], 0, p.status), abort_flag);
+    if (ok) {
+      tc::fence_after_sync();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      T *orow = out + (static_cast<int64_t>(q_start + t0 + x * TQ + tok) * p.num_q_heads + kvh * G + r % G) * 128;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        if (my_nkv > 0) {
+          tc::tmem_ld32(tO + c * 32, o);
+          tc::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (rvalid) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            w.x = pack2(o[i] * inv, o[i + 1] * inv, kBf16);
+            w.y = pack2(o[i + 2] * inv, o[i + 3] * inv, kBf16);
+            w.z = pack2(o[i + 4] * inv, o[i + 5] * inv, kBf16);
+            w.w = pack2(o[i + 6] * inv, o[i + 7] * inv, kBf16);
+            *reinterpret_cast<uint4 *>(orow + c * 32 + i) = w;
+          }
+        }
+      }
+    } else if (lane == 0) {
+      *(volatile int *)abort_flag = 1;
+    }
+  }
+
+  pdl_launch_dependents();
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 9) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
 namespace {
 
 // 3-D map (x = D columns, y = heads, z = rows) with a {64, box_y, box_z} box.
@@ -516,6 +900,40 @@ cudaError_t launch_tg(PrefillTcParams &p, int num_kv_heads, int64_t num_seqs, in
   constexpr int TQ = 128 / G;
   const dim3 grid((max_seqlen_q + TQ - 1) / TQ, num_kv_heads, static_cast<unsigned>(num_seqs));
   return launch_pdl(kern, grid, dim3(kThreads), kSmemBytes, stream, p);
+}
+
+template <typename T, int G>
+cudaError_t launch_tg2(PrefillTcParams &p, int num_kv_heads, int64_t num_seqs, int32_t max_seqlen_q,
+                       cudaStream_t stream) {
+  auto kern = prefill_tc2_kernel<T, G>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes2);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  constexpr int TQ = 128 / G;
+  const dim3 grid((max_seqlen_q + 2 * TQ - 1) / (2 * TQ), num_kv_heads, static_cast<unsigned>(num_seqs));
+  return launch_pdl(kern, grid, dim3(kThreads2), kSmemBytes2, stream, p);
+}
+
+// Two query tiles per CTA unless MICROINFER_B200_PREFILL=tc1 pins the
+// one-tile kernel.
+bool prefill_two_tiles() {
+  static const bool two = [] {
+    const char *v = std::getenv("MICROINFER_B200_PREFILL");
+    return !(v != nullptr && std::strcmp(v, "tc1") == 0);
+  }();
+  return two;
+}
+
+template <typename T, int G>
+cudaError_t launch_any(PrefillTcParams &p, int num_kv_heads, int64_t num_seqs, int32_t max_seqlen_q,
+                       cudaStream_t stream) {
+  return prefill_two_tiles() ? launch_tg2<T, G>(p, num_kv_heads, num_seqs, max_seqlen_q, stream)
+                             : launch_tg<T, G>(p, num_kv_heads, num_seqs, max_seqlen_q, stream);
 }
 
 }  // namespace
@@ -568,17 +986,17 @@ cudaError_t launch_prefill_tc(const AttnParams &a, int dtype, int G, int32_t max
   const int64_t n = a.num_seqs;
   if (dtype == MI_DTYPE_BFLOAT16) {
     switch (G) {
-      case 1: return launch_tg<__nv_bfloat16, 1>(p, a.num_kv_heads, n, max_seqlen_q, stream);
-      case 2: return launch_tg<__nv_bfloat16, 2>(p, a.num_kv_heads, n, max_seqlen_q, stream);
-      case 4: return launch_tg<__nv_bfloat16, 4>(p, a.num_kv_heads, n, max_seqlen_q, stream);
-      default: return launch_tg<__nv_bfloat16, 8>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+      case 1: return launch_any<__nv_bfloat16, 1>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+      case 2: return launch_any<__nv_bfloat16, 2>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+      case 4: return launch_any<__nv_bfloat16, 4>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+      default: return launch_any<__nv_bfloat16, 8>(p, a.num_kv_heads, n, max_seqlen_q, stream);
     }
   }
   switch (G) {
-    case 1: return launch_tg<__half, 1>(p, a.num_kv_heads, n, max_seqlen_q, stream);
-    case 2: return launch_tg<__half, 2>(p, a.num_kv_heads, n, max_seqlen_q, stream);
-    case 4: return launch_tg<__half, 4>(p, a.num_kv_heads, n, max_seqlen_q, stream);
-    default: return launch_tg<__half, 8>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+    case 1: return launch_any<__half, 1>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+    case 2: return launch_any<__half, 2>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+    case 4: return launch_any<__half, 4>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+    default: return launch_any<__half, 8>(p, a.num_kv_heads, n, max_seqlen_q, stream);
   }
 }
 
