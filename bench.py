@@ -354,6 +354,14 @@ def _prefill_batch(workload: str, device, g):
                 slots=torch.tensor(slots, dtype=torch.int32, device=device))
 
 
+def prefill_kernel_name() -> str:
+    """The tcgen05 prefill kernel the library launches (MICROINFER_B200_PREFILL=tc1 pins the
+    one-tile kernel)."""
+    if os.environ.get("MICROINFER_B200_PREFILL") == "tc1":
+        return "prefill_tc_kernel (tcgen05, one 128-row query tile per CTA)"
+    return "prefill_tc2_kernel (tcgen05, two 128-row query tiles per CTA sharing K/V)"
+
+
 def measure_prefill(device, workload: str, layers: int = 28, reps: int = 10):
     """Store + paged prefill per layer (one attention launch for the whole batch).
 
@@ -408,7 +416,7 @@ def measure_prefill(device, workload: str, layers: int = 28, reps: int = 10):
     res = {"workload": ("BASELINE configs[2]: 24 decode + 8x512 prefill chunks, one launch"
                         if workload == "mixed" else
                         "BASELINE configs[3]: 64 x 128-token suffix on a shared 1024 prefix"),
-           "kernel": "prefill_tc_kernel (tcgen05)", "layers": layers,
+           "kernel": prefill_kernel_name(), "layers": layers,
            "us_per_layer": round(ms_layer * 1e3, 2), "flops_per_layer": flops,
            "tflops": round(tflops, 1), "tensor_frac": round(tflops / peaks["bf16_tflops"], 4),
            "peak_source": f"bf16_tflops of {src}", "store_tokens": tokens}
