@@ -32,6 +32,7 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 LAYERS, HQ, HKV, D, BS, NB, NSEQ = 28, 16, 8, 128, 16, 1024, 8
+E2E_GROUP = 7  # layers per input copy on the end-to-end path
 CTX_LO, CTX_HI = 128, 512
 METRIC = "paged decode attn HBM GB/s (Qwen3-0.6B decode step, store+decode x28 layers)"
 WORKLOAD = "BASELINE configs[1]: Qwen3-0.6B decode step, bf16, 28 layers, batch 8/GPU"
@@ -602,32 +603,59 @@ def run_ours(args):
 
     # --- per-rank shard: own pool, own 8 sequences -------------------------
     ctx, table, slots = make_batch(1000 + rank, device)
-    ctx_d, table_d, slots_d = ctx.to(device), table.to(device), slots.to(device)
+    # The step's int32 inputs (lengths, tables, slots) share one device buffer so the
+    # end-to-end path moves them in one copy.
+    meta_d = torch.empty(ctx.numel() + table.numel() + slots.numel(), dtype=torch.int32,
+                         device=device)
+    ctx_d = meta_d[: ctx.numel()]
+    table_d = meta_d[ctx.numel(): ctx.numel() + table.numel()].view(table.shape)
+    slots_d = meta_d[ctx.numel() + table.numel():]
+    ctx_d.copy_(ctx)
+    table_d.copy_(table)
+    slots_d.copy_(slots)
     pool = mi.KVCache(LAYERS, NB, BS, HKV, D, dtype=torch.bfloat16, device=device)
     g = torch.Generator(device=device).manual_seed(rank)
     pool.keys.normal_(generator=g).mul_(0.5)
     pool.values.normal_(generator=g).mul_(0.5)
-    q = torch.randn(LAYERS, NSEQ, HQ, D, generator=g, device=device).to(torch.bfloat16)
-    kn = torch.randn(LAYERS, NSEQ, HKV, D, generator=g, device=device).to(torch.bfloat16)
-    vn = torch.randn(LAYERS, NSEQ, HKV, D, generator=g, device=device).to(torch.bfloat16)
-    out = torch.empty_like(q)
+    q_all = torch.randn(LAYERS, NSEQ, HQ, D, generator=g, device=device).to(torch.bfloat16)
+    kn_all = torch.randn(LAYERS, NSEQ, HKV, D, generator=g, device=device).to(torch.bfloat16)
+    vn_all = torch.randn(LAYERS, NSEQ, HKV, D, generator=g, device=device).to(torch.bfloat16)
+    # Per-layer inputs packed by groups of E2E_GROUP layers, [q | k_new | v_new] per group,
+    # so the end-to-end path copies one buffer per group.
+    qn, kvn = E2E_GROUP * NSEQ * HQ * D, E2E_GROUP * NSEQ * HKV * D
+    pk_d = torch.empty(LAYERS // E2E_GROUP, qn + 2 * kvn, dtype=torch.bfloat16, device=device)
+    q, kn, vn = [], [], []
+    for gi in range(LAYERS // E2E_GROUP):
+        lo, hi = gi * E2E_GROUP, (gi + 1) * E2E_GROUP
+        pk_d[gi, :qn].copy_(q_all[lo:hi].reshape(-1))
+        pk_d[gi, qn:qn + kvn].copy_(kn_all[lo:hi].reshape(-1))
+        pk_d[gi, qn + kvn:].copy_(vn_all[lo:hi].reshape(-1))
+        q += list(pk_d[gi, :qn].view(E2E_GROUP, NSEQ, HQ, D).unbind(0))
+        kn += list(pk_d[gi, qn:qn + kvn].view(E2E_GROUP, NSEQ, HKV, D).unbind(0))
+        vn += list(pk_d[gi, qn + kvn:].view(E2E_GROUP, NSEQ, HKV, D).unbind(0))
+    del q_all, kn_all, vn_all
+    out = torch.empty(LAYERS, NSEQ, HQ, D, dtype=torch.bfloat16, device=device)
     tokens = torch.empty(NSEQ, dtype=torch.int32, device=device)
     decode_kernel, split, _ = mi.decode_plan(NSEQ, HQ, HKV, D, torch.bfloat16, BS, 0, device,
                                              table_d.shape[1])
     views = [pool.layer(i) for i in range(LAYERS)]
 
-    def attention_layers():
+    def attention_layers(layers=range(LAYERS)):
         # store_kvcache fused into paged decode: one launch per layer
-        for i, view in enumerate(views):
+        for i in layers:
+            view = views[i]
             # Layer i+1's launch only follows layer i's decode, which writes neither
             # layer i+1's pool nor the tables: its pages may load early (PDL).
             mi.paged_decode_store(q[i], view.keys, view.values, table_d, ctx_d, kn[i], vn[i],
                                   slots_d, split_k=split, out=out[i], early_kv=True)
 
-    def layer_loop():
-        attention_layers()
+    def sample():
         # stand-in sampler: one int32 token id per sequence from the last layer
         tokens.copy_(out[-1, :, 0, :].float().argmax(-1))
+
+    def layer_loop():
+        attention_layers()
+        sample()
 
     decode_only = attention_layers
 
@@ -707,26 +735,62 @@ def run_ours(args):
     achieved = (dec_b + st_b) / (decode_launch_ms * 1e-3) / 1e9
 
     # --- e2e: host buffers through the public API ----------------------------
-    h_q = torch.empty_like(q, device="cpu").pin_memory()
-    h_kn = torch.empty_like(kn, device="cpu").pin_memory()
-    h_vn = torch.empty_like(vn, device="cpu").pin_memory()
-    h_ctx = ctx.clone().pin_memory()
-    h_table = table.clone().pin_memory()
-    h_slots = slots.clone().pin_memory()
+    # Every step copies its inputs in from pinned host memory and its results (the
+    # attention outputs of all layers and the gathered token ids) back, inside the
+    # timed region.  Each group of E2E_GROUP layers has one packed input buffer, copied
+    # on a side stream while the previous group computes; a group's outputs go back on
+    # a third stream as soon as it finishes.
+    groups = LAYERS // E2E_GROUP
+    h_pk = pk_d.cpu().pin_memory()
+    h_meta = meta_d.cpu().pin_memory()
     h_out = torch.empty_like(out, device="cpu").pin_memory()
-    h_q.copy_(q.cpu()); h_kn.copy_(kn.cpu()); h_vn.copy_(vn.cpu())
-    h2d = sum(t.numel() * t.element_size() for t in (h_q, h_kn, h_vn, h_ctx, h_table, h_slots))
-    d2h = h_out.numel() * h_out.element_size() + tokens.numel() * 4 * world
+    tok_all = torch.empty(world * NSEQ, dtype=torch.int32, device=device)
+    h_tok = torch.empty(world * NSEQ, dtype=torch.int32).pin_memory()
+    h2d = h_pk.numel() * h_pk.element_size() + h_meta.numel() * h_meta.element_size()
+    d2h = h_out.numel() * h_out.element_size() + h_tok.numel() * h_tok.element_size()
+    gstream = torch.cuda.Stream(device)
+    gstream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(gstream):
+        for gi in range(groups):
+            attention_layers(range(gi * E2E_GROUP, (gi + 1) * E2E_GROUP))
+        sample()
+    torch.cuda.current_stream(device).wait_stream(gstream)
+    torch.cuda.synchronize(device)
+    ggraphs = []
+    for gi in range(groups):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            attention_layers(range(gi * E2E_GROUP, (gi + 1) * E2E_GROUP))
+            if gi == groups - 1:
+                sample()
+        ggraphs.append(gr)
+    h2d_stream, d2h_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev_in = [torch.cuda.Event() for _ in range(groups)]
+    ev_done = [torch.cuda.Event() for _ in range(groups)]
 
     def e2e_step():
-        q.copy_(h_q, non_blocking=True)
-        kn.copy_(h_kn, non_blocking=True)
-        vn.copy_(h_vn, non_blocking=True)
-        ctx_d.copy_(h_ctx, non_blocking=True)
-        table_d.copy_(h_table, non_blocking=True)
-        slots_d.copy_(h_slots, non_blocking=True)
-        step()
-        h_out.copy_(out, non_blocking=True)
+        h2d_stream.wait_stream(cur)  # the previous step no longer reads the inputs
+        with torch.cuda.stream(h2d_stream):
+            meta_d.copy_(h_meta, non_blocking=True)
+            for gi in range(groups):
+                pk_d[gi].copy_(h_pk[gi], non_blocking=True)
+                ev_in[gi].record(h2d_stream)
+        for gi in range(groups):
+            cur.wait_event(ev_in[gi])
+            ggraphs[gi].replay()
+            ev_done[gi].record(cur)
+            d2h_stream.wait_event(ev_done[gi])
+            with torch.cuda.stream(d2h_stream):
+                lo, hi = gi * E2E_GROUP, (gi + 1) * E2E_GROUP
+                h_out[lo:hi].copy_(out[lo:hi], non_blocking=True)
+        if world > 1:
+            dist.all_gather_into_tensor(tok_all, tokens)
+        else:
+            tok_all.copy_(tokens)
+        d2h_stream.wait_stream(cur)
+        with torch.cuda.stream(d2h_stream):
+            h_tok.copy_(tok_all, non_blocking=True)
+        cur.wait_stream(d2h_stream)  # the step ends with its results on the host
 
     for _ in range(3):
         e2e_step()
@@ -780,7 +844,9 @@ def run_ours(args):
                          "step_frac": round(value / world / peaks["hbm_gbs"], 4)},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
-                    "path": "pinned host inputs -> microinfer_b200 API (C ABI) -> host output"},
+                    "path": ("pinned host inputs -> microinfer_b200 API (C ABI) -> host outputs; "
+                             f"inputs copied per group of {E2E_GROUP} layers on a side stream while "
+                             "the previous group computes, outputs copied back per group")},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
         }
