@@ -118,7 +118,8 @@ MI_API size_t mi_paged_decode_workspace_bytes(int64_t num_seqs, int32_t num_q_he
                                        int32_t head_dim, int32_t num_splits);
 
 /*
- * Split count the decode launcher uses when the caller passes num_splits=0.
+ * Split count the decode launcher uses when the caller passes num_splits=0
+ * (the mma kernel differs for larger batches, see mi_paged_decode_plan).
  * When num_seqs * num_kv_heads fits in half the SMs, the layer's CTAs stay
  * within that half (one CTA per SM), so the next layer's CTAs fit beside
  * them and request their pages early; with `max_context_hint` > 0 each split
@@ -138,7 +139,7 @@ MI_API int mi_paged_decode_default_splits(int64_t num_seqs, int32_t num_kv_heads
  * num_splits > 1 needs `workspace` (mi_paged_decode_workspace_bytes,
  * zero-filled before its first use); the last split of each (sequence,
  * kv head) merges the states in the same launch.  num_splits == 0 picks
- * mi_paged_decode_default_splits.
+ * the split count of mi_paged_decode_plan.
  * Query and out are contiguous [num_seqs, num_q_heads, head_dim].
  */
 MI_API int mi_paged_decode(void *out, const void *query, const void *key_cache,
@@ -159,11 +160,14 @@ MI_API int mi_paged_decode_uses_workspace(int32_t num_splits);
 /*
  * Launch plan of mi_paged_decode / mi_paged_decode_store for a shape with
  * 16-byte aligned tensors: returns the kernel (1 generic, 2 SIMT bulk-copy,
- * 3 tcgen05 tensor-core) and writes the split count it will use for
- * `num_splits` (0 = automatic) and the workspace bytes the caller must pass.
- * The tensor-core kernel is chosen when the block table can address at least
- * 2048 keys per sequence (block_table_stride * block_size); shorter contexts
- * run the SIMT kernel.  MICROINFER_B200_DECODE=simt|tc pins one.
+ * 3 tcgen05 swap-AB, 4 warp-level mma tensor-core) and writes the split
+ * count it will use for `num_splits` (0 = automatic) and the workspace bytes
+ * the caller must pass.  The mma kernel runs bf16/fp16 with head_dim 64 or
+ * 128, a GQA group of 1, 2, 4 or 8 and block_size a multiple of 16; other
+ * fast shapes run the SIMT kernel; MICROINFER_B200_DECODE=simt|tc|mma pins
+ * one.  Automatic splits are mi_paged_decode_default_splits, except that the
+ * mma kernel (one CTA per SM) takes one split once num_seqs * num_kv_heads
+ * exceeds half the SMs.
  */
 MI_API int mi_paged_decode_plan(int64_t num_seqs, int32_t num_q_heads,
                          int32_t num_kv_heads, int32_t head_dim,

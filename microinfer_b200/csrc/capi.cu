@@ -287,6 +287,13 @@ int decode_splits_for(int kernel, int64_t num_seqs, int num_kv_heads, int num_sp
                       int64_t ctx_bound) {
   if (num_splits > 0) return num_splits;
   if (kernel == kDecodeGeneric) return 1;
+  if (kernel == kDecodeMma && 2 * num_seqs * num_kv_heads > sm_count_of(dev)) {
+    // The mma kernel holds one CTA per SM: once the (sequence, kv head) pairs
+    // fill more than half the SMs, a second split only adds a merge through
+    // global memory and a second wave (batch 16, Qwen3-0.6B heads: 1 split
+    // 6.2-45 us per layer for contexts 512-4096, 2 splits 13-52 us).
+    return 1;
+  }
   if (kernel == kDecodeSimt || kernel == kDecodeMma) {
     const int64_t hint = ctx_bound > INT32_MAX ? INT32_MAX : ctx_bound;
     return mi_paged_decode_default_splits(num_seqs, num_kv_heads, static_cast<int32_t>(hint), dev);

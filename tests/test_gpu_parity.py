@@ -127,8 +127,8 @@ def test_decode_split_k_matches_reference(name, split_k):
 
 
 @pytest.mark.parametrize("name", [c for c in PAGED if cases.kind(c) == "decode"])
-@pytest.mark.parametrize("split_k,early_kv", [(1, False), (4, False), (16, False), (4, True),
-                                              (37, True)])
+@pytest.mark.parametrize("split_k,early_kv", [(1, False), (2, False), (2, True), (4, False),
+                                              (16, False), (4, True), (37, True)])
 def test_fused_store_decode_matches_reference(name, split_k, early_kv):
     """store_kvcache fused into the decode launch: same cache bytes, same output."""
     case = cases.build(name)
@@ -187,6 +187,19 @@ def test_fused_store_with_only_the_new_token(width, split_k, early_kv):
     torch.testing.assert_close(out, expected, atol=0, rtol=0)
     torch.testing.assert_close(kc[table[:, 0].long(), 0], kn, atol=0, rtol=0)
     torch.testing.assert_close(vc[table[:, 0].long(), 0], vn, atol=0, rtol=0)
+
+
+def test_mma_plan_takes_one_split_past_half_the_sms():
+    """The mma kernel holds one CTA per SM: once the (sequence, kv head) pairs
+    exceed half the SMs, the automatic plan uses no split (and no workspace)."""
+    if "MICROINFER_B200_DECODE" in os.environ:
+        pytest.skip("kernel pinned")
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    n = sms // 16 + 1  # 2 * n * 8 kv heads > sms
+    kernel, split, ws = mi.decode_plan(n, 16, 8, 128, torch.bfloat16, 16, 0, "cuda", 32)
+    assert (kernel, split, ws) == ("mma", 1, 0)
+    kernel, split, _ = mi.decode_plan(8, 16, 8, 128, torch.bfloat16, 16, 0, "cuda", 256)
+    assert kernel == "mma" and split >= 2  # small batch, 4096-key tables: splits
 
 
 @pytest.mark.parametrize("width", [40, 160])  # 640 / 2560-key table bound
