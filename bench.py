@@ -635,7 +635,11 @@ def run_ours(args):
         vn += list(pk_d[gi, qn + kvn:].view(E2E_GROUP, NSEQ, HKV, D).unbind(0))
     del q_all, kn_all, vn_all
     out = torch.empty(LAYERS, NSEQ, HQ, D, dtype=torch.bfloat16, device=device)
-    tokens = torch.empty(NSEQ, dtype=torch.int32, device=device)
+    # Sampled token ids, double-buffered: step k writes buffer k % 2 while the
+    # all_gather of step k-1 (off the attention path, on its own stream) reads
+    # the other one.
+    tokens_buf = torch.empty(2, NSEQ, dtype=torch.int32, device=device)
+    tokens = tokens_buf[0]
     decode_kernel, split, _ = mi.decode_plan(NSEQ, HQ, HKV, D, torch.bfloat16, BS, 0, device,
                                              table_d.shape[1])
     views = [pool.layer(i) for i in range(LAYERS)]
@@ -649,13 +653,13 @@ def run_ours(args):
             mi.paged_decode_store(q[i], view.keys, view.values, table_d, ctx_d, kn[i], vn[i],
                                   slots_d, split_k=split, out=out[i], early_kv=True)
 
-    def sample():
+    def sample(slot=0):
         # stand-in sampler: one int32 token id per sequence from the last layer
-        tokens.copy_(out[-1, :, 0, :].float().argmax(-1))
+        tokens_buf[slot].copy_(out[-1, :, 0, :].float().argmax(-1))
 
-    def layer_loop():
+    def layer_loop(slot=0):
         attention_layers()
-        sample()
+        sample(slot)
 
     decode_only = attention_layers
 
@@ -668,27 +672,46 @@ def run_ours(args):
             decode_only()
     torch.cuda.current_stream(device).wait_stream(stream)
     torch.cuda.synchronize(device)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        layer_loop()
+    graphs = []
+    for slot in range(2):
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            layer_loop(slot)
+        graphs.append(gr)
+    graph = graphs[0]
     dgraph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(dgraph):
         decode_only()
-    gathered = [torch.empty_like(tokens) for _ in range(world)]
+    cur = torch.cuda.current_stream(device)
+    gathered = torch.empty(2, world * NSEQ, dtype=torch.int32, device=device)
+    ag_stream = torch.cuda.Stream(device)
+    ag_ready = [torch.cuda.Event() for _ in range(2)]
+    ag_done = [torch.cuda.Event() for _ in range(2)]
 
-    def step():
-        graph.replay()
+    def step(k):
+        # One decode step: 28 layers + sampler into tokens_buf[k % 2], then the
+        # all_gather of those token ids (for the scheduler, off the attention path)
+        # on its own stream, overlapping the next step's layers; step k+2 reuses
+        # the buffer only after that gather is done.
+        slot = k & 1
         if world > 1:
-            dist.all_gather(gathered, tokens)
+            cur.wait_event(ag_done[slot])
+        graphs[slot].replay()
+        if world > 1:
+            ag_ready[slot].record(cur)
+            ag_stream.wait_event(ag_ready[slot])
+            with torch.cuda.stream(ag_stream):
+                dist.all_gather_into_tensor(gathered[slot], tokens_buf[slot])
+            ag_done[slot].record(ag_stream)
 
-    for _ in range(max(3, args.warmup)):
-        step()
+    for k in range(max(3, args.warmup)):
+        step(k)
+    cur.wait_stream(ag_stream)
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
 
     # --- timed region: exactly K steps ---------------------------------------
-    cur = torch.cuda.current_stream(device)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     t_all0, t_all1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -697,8 +720,9 @@ def run_ours(args):
         t_all0.record(cur)
         for k in range(args.steps):
             starts[k].record(cur)
-            step()
+            step(k)
             ends[k].record(cur)
+        cur.wait_stream(ag_stream)  # the last step's gather ends inside the timed region
         t_all1.record(cur)
         torch.cuda.synchronize(device)
         # keep sampling clocks over ~1 s of the same step (not timed)
@@ -858,7 +882,7 @@ def run_ours(args):
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
-    del graph, dgraph
+    del graph, graphs, dgraph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
