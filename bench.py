@@ -214,8 +214,10 @@ def measure_long_b1(device, reps: int = 20):
 
     def run():
         for i, view in enumerate(views):
+            # as in the config-2 step: layer i's decode writes neither layer i+1's pool
+            # nor the table, so layer i+1's pages may load early
             mi.paged_decode_store(q[i], view.keys, view.values, table, ctx, kn[i], kn[i], slots,
-                                  split_k=split, out=out[i])
+                                  split_k=split, out=out[i], early_kv=True)
 
     run()
     torch.cuda.synchronize(device)
@@ -919,7 +921,7 @@ def run_profile(args):
             for i in range(layers):
                 view = pool.layer(i)
                 mi.paged_decode_store(q[i], view.keys, view.values, table, ctx, kn[i], kn[i],
-                                      slots, split_k=split)
+                                      slots, split_k=split, early_kv=True)
         torch.cuda.synchronize(device)
         mi.check_device_status(device)
         from oracle.paged_oracle import decode_bytes

@@ -14,9 +14,9 @@
 // own 16-key chunks (ids strided over splits and warps) through a 3-stage
 // ring: per chunk one TMA copy per 64-dim half for K and for V (3-D tensor
 // map over [slots][Hkv][D], box {64, 1, 16}, 128-byte swizzle, so ldmatrix
-// reads are bank-conflict free).  Pages beyond the ring are prefetched into
-// L2 before the dependency wait (early_kv), the block table in batches of
-// 32 chunks loaded a batch ahead.  Online softmax in the log2 domain with
+// reads are bank-conflict free); with early_kv the ring fills before the
+// dependency wait.  The block table is read in batches of 32 chunks loaded
+// a batch ahead.  Online softmax in the log2 domain with
 // lazy rescale; the warps merge in shared memory, the splits through the
 // workspace (split_merge.cuh).  With the fused store, this step's token is
 // folded in as a one-key chunk built from k_new/v_new (the last item of the
@@ -49,7 +49,6 @@ constexpr unsigned kAll = 0xffffffffu;
 constexpr int kChunk = 16;  // keys per chunk
 constexpr int kStagesM = 3;
 constexpr int kWarpsM = 8;
-constexpr int kAheadM = 4;  // chunks per warp prefetched into L2 beyond the ring
 
 template <int D>
 struct MmaCfg {
@@ -182,7 +181,6 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     const int64_t col = static_cast<int64_t>(ci) * kChunk / p.block_size;
     return col < p.bt_stride ? __ldg(table + col) : -1;
   };
-  constexpr int kWin = kStagesM + kAheadM;
   // Pages in batches of 32 loop iterations: lane L holds the page of
   // iteration 32 * batch + L; the next batch is loaded a whole batch ahead
   // and page(it) is a shuffle, so no register move waits on a recent load.
@@ -239,26 +237,15 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     }
   };
 
-  // Prologue: fill the ring, warm L2 with the next chunks, then wait on the
-  // preceding kernel (early_kv) and let the next one start its prologue.
+  // Prologue: fill the ring, then wait on the preceding kernel (early_kv) and
+  // let the next one start its prologue.  (An L2 prefetch of the chunks past
+  // the ring measured slower: 3848 vs 4131 GB/s at batch 1 x 32K.)
   int issued = 0;
 #pragma unroll
   for (int s = 0; s < kStagesM; ++s) {
     if (s < my_n) {
       issue(chunk_of(s), s, checked(page(0, s)));
       ++issued;
-    }
-  }
-#pragma unroll
-  for (int j = kStagesM; j < kWin; ++j) {
-    const int32_t blk = page(0, j);
-    if (lane == 0 && j < my_n && blk >= 0 && blk < p.num_blocks) {
-      const int row = row_of(chunk_of(j), blk);
-#pragma unroll
-      for (int h = 0; h < C::kHalves; ++h) {
-        tc::tma_prefetch_l2_3d(&P.tmap_k, h * 64, kvh, row);
-        tc::tma_prefetch_l2_3d(&P.tmap_v, h * 64, kvh, row);
-      }
     }
   }
   if (p.early_kv) {
@@ -418,22 +405,9 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     }
     __syncwarp();  // zeroed rows and the token's row are visible to every lane
     process(kt, vt, valid);
-    if (it < my_n) {
-      // Refill the stage just consumed, and keep the rolling L2 prefetch
-      // kWin - 1 chunks ahead (the prologue covered the first kWin).
-      if (it + kStagesM < my_n) {
-        issue(chunk_of(it + kStagesM), it % kStagesM, checked(page(it, it + kStagesM)));
-        ++issued;
-      }
-      const int32_t blk = page(it, it + kWin - 1);
-      if (it > 0 && lane == 0 && it + kWin - 1 < my_n && blk >= 0 && blk < p.num_blocks) {
-        const int row = row_of(chunk_of(it + kWin - 1), blk);
-#pragma unroll
-        for (int h = 0; h < C::kHalves; ++h) {
-          tc::tma_prefetch_l2_3d(&P.tmap_k, h * 64, kvh, row);
-          tc::tma_prefetch_l2_3d(&P.tmap_v, h * 64, kvh, row);
-        }
-      }
+    if (it + kStagesM < my_n) {  // refill the stage just consumed
+      issue(chunk_of(it + kStagesM), it % kStagesM, checked(page(it, it + kStagesM)));
+      ++issued;
     }
     if ((it & 31) == 31) {  // the next iteration starts batch (it + 1) / 32
       pg_cur = pg_nxt;
