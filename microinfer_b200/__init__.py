@@ -10,6 +10,8 @@ reference's attention-backend interface:
 * ``layer.paged_attention.varlen_prefill``           - dense (no-prefix) prefill
 * ``layer.paged_attention.gather_paged_kv``          - block-table gather
 * ``worker.kv_cache.copy_blocks``                    - copy-on-write of pages
+* ``worker.block_manager.CowBlockManager``           - refcounted pages, shared partial
+  blocks and the (src, dst) copies that ``copy_blocks`` issues
 * ``layer.paged_attention.paged_attention_meta``     - backend dispatch
 
 ``install()`` rebinds a live ``microinfer`` import onto these entry points.
@@ -28,13 +30,16 @@ from microinfer_b200.layer.paged_attention import (
     select_split_k,
     varlen_prefill,
 )
+from microinfer_b200.worker.block_manager import CowBlockManager, apply_copies
 from microinfer_b200.worker.kv_cache import KVCache, LayerKVCache, copy_blocks
 from microinfer_b200.worker.kv_store import store_kv, store_kv_slots
 
 __all__ = [
     "AttentionMetadata",
+    "CowBlockManager",
     "KVCache",
     "LayerKVCache",
+    "apply_copies",
     "check_device_status",
     "copy_blocks",
     "decode_plan",

@@ -189,6 +189,58 @@ def test_fused_store_with_only_the_new_token(width, split_k, early_kv):
     torch.testing.assert_close(vc[table[:, 0].long(), 0], vn, atol=0, rtol=0)
 
 
+class _Seq:
+    def __init__(self, num_tokens):
+        self.num_tokens = num_tokens
+        self.block_table = []
+
+
+def test_forked_sequences_copy_on_write_then_decode_in_isolation():
+    """Two sequences share a partial page (CowBlockManager.fork); each appends its
+    own token.  apply_copies issues the page copy on the device (every layer),
+    then the fused store+decode writes and attends: each sequence's output is
+    attention over its own 21 tokens only, in every layer."""
+    bs, hkv, hq, d, nb, layers = 16, 8, 16, 128, 16, 2
+    gen = torch.Generator(device="cuda").manual_seed(21)
+    cache = mi.KVCache(layers, nb, bs, hkv, d, dtype=torch.bfloat16, device="cuda")
+    m = mi.CowBlockManager(nb, bs)
+    a = _Seq(20)
+    m.allocate(a)
+    hist = [(torch.randn(20, hkv, d, generator=gen, device="cuda").to(torch.bfloat16),
+             torch.randn(20, hkv, d, generator=gen, device="cuda").to(torch.bfloat16))
+            for _ in range(layers)]
+    pos = torch.arange(20)
+    slots = (torch.tensor(a.block_table)[pos // bs] * bs + pos % bs).to(torch.int32).cuda()
+    for li in range(layers):
+        cache.layer(li).write_slots(slots, *hist[li])
+    b = _Seq(20)
+    m.fork(a, b)
+    new_slots = torch.tensor([m.prepare_append(a), m.prepare_append(b)], dtype=torch.int32)
+    assert mi.apply_copies(m, cache) == 1  # b's copy of the shared partial page
+    a.num_tokens = b.num_tokens = 21
+    width = max(len(a.block_table), len(b.block_table))
+    table = torch.full((2, width), -1, dtype=torch.int32)
+    table[0, :len(a.block_table)] = torch.tensor(a.block_table)
+    table[1, :len(b.block_table)] = torch.tensor(b.block_table)
+    ctx = torch.tensor([21, 21], dtype=torch.int32, device="cuda")
+    for li in range(layers):
+        q = torch.randn(2, hq, d, generator=gen, device="cuda").to(torch.bfloat16)
+        kn = torch.randn(2, hkv, d, generator=gen, device="cuda").to(torch.bfloat16)
+        vn = torch.randn(2, hkv, d, generator=gen, device="cuda").to(torch.bfloat16)
+        view = cache.layer(li)
+        out = mi.paged_decode_store(q, view.keys, view.values, table.cuda(), ctx, kn, vn,
+                                    new_slots.cuda())
+        torch.cuda.synchronize()
+        for i in range(2):
+            keys = torch.cat([hist[li][0], kn[i:i + 1]]).float()
+            vals = torch.cat([hist[li][1], vn[i:i + 1]]).float()
+            kh = keys.repeat_interleave(hq // hkv, dim=1)  # [21, hq, d]
+            vh = vals.repeat_interleave(hq // hkv, dim=1)
+            sc = torch.einsum("hd,thd->ht", q[i].float(), kh) * d ** -0.5
+            want = torch.einsum("ht,thd->hd", torch.softmax(sc, dim=-1), vh)
+            torch.testing.assert_close(out[i].float(), want, atol=2e-2, rtol=1e-2)
+
+
 def test_mma_plan_takes_one_split_past_half_the_sms():
     """The mma kernel holds one CTA per SM: once the (sequence, kv head) pairs
     exceed half the SMs, the automatic plan uses no split (and no workspace)."""
