@@ -431,6 +431,105 @@ def measure_prefill(device, workload: str, layers: int = 28, reps: int = 10):
     return res
 
 
+def _prologue_inputs(device, layers: int, tokens: int, g):
+    """Per layer: packed qkv rows [T, (Hq + 2 Hkv) * D], norm weights and a pool
+    with room for every token; one RotaryCache-style fp32 table shared by all."""
+    import torch
+
+    import microinfer_b200 as mi
+
+    nb = (tokens + BS - 1) // BS
+    pool = mi.KVCache(layers, nb, BS, HKV, D, dtype=torch.bfloat16, device=device)
+    qkv = torch.randn(layers, tokens, (HQ + 2 * HKV) * D, generator=g,
+                      device=device).to(torch.bfloat16)
+    qw = (torch.rand(layers, D, generator=g, device=device) + 0.5).to(torch.bfloat16)
+    kw = (torch.rand(layers, D, generator=g, device=device) + 0.5).to(torch.bfloat16)
+    max_pos = 40960
+    inv_freq = 1.0 / (1e6 ** (torch.arange(0, D, 2, device=device).float() / D))
+    ang = torch.outer(torch.arange(max_pos, device=device).float(), inv_freq)
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+    positions = torch.randint(0, max_pos, (tokens,), generator=g, device=device)
+    slots = torch.randperm(nb * BS, generator=g, device=device)[:tokens].to(torch.int32)
+    return pool, qkv, qw, kw, cos, sin, positions, slots
+
+
+def prologue_bytes(tokens: int) -> int:
+    """Algorithmic HBM bytes of one prologue launch (bf16): the packed qkv row read
+    once, q written once, k and v written once into the pool, the token's cos/sin
+    row (fp32) and its position and slot read once."""
+    row = (HQ + 2 * HKV) * D * 2
+    return tokens * (row + HQ * D * 2 + 2 * HKV * D * 2 + D * 4 + 8 + 4)
+
+
+def measure_prologue(device, tokens: int = 8192, layers: int = 8, reps: int = 20):
+    """Fused q/k RMSNorm + RoPE + k/v store (one launch per layer) against the
+    reference's eager op sequence (FuseLayerNorm x2, RotaryCache.apply x2, slot
+    store) written as torch ops, both over `layers` distinct layer buffers so the
+    working set (layers x 128 MB) is far larger than L2."""
+    import torch
+
+    import microinfer_b200 as mi
+
+    g = torch.Generator(device=device).manual_seed(21)
+    pool, qkv, qw, kw, cos, sin, positions, slots = _prologue_inputs(device, layers, tokens, g)
+    q_out = torch.empty(layers, tokens, HQ, D, dtype=torch.bfloat16, device=device)
+    views = [pool.layer(i) for i in range(layers)]
+    sl = slots.long()
+
+    def fused():
+        for i, view in enumerate(views):
+            mi.qk_norm_rope_store(qkv[i], qw[i], kw[i], positions, cos, sin, view.keys,
+                                  view.values, slots, num_q_heads=HQ, num_kv_heads=HKV, eps=1e-6,
+                                  out=q_out[i])
+
+    def eager():
+        c, s_ = cos[positions].unsqueeze(1), sin[positions].unsqueeze(1)
+
+        def norm(x, w):
+            xf = x.float()
+            return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()).to(
+                torch.bfloat16)
+
+        def rope(x):
+            a, b = x.float().chunk(2, dim=-1)
+            return torch.cat((a * c - b * s_, b * c + a * s_), dim=-1).to(torch.bfloat16)
+
+        for i, view in enumerate(views):
+            x = qkv[i].view(tokens, HQ + 2 * HKV, D)
+            q_out[i].copy_(rope(norm(x[:, :HQ], qw[i])))
+            k = rope(norm(x[:, HQ:HQ + HKV], kw[i]))
+            view.keys.view(-1, HKV, D).index_copy_(0, sl, k)
+            view.values.view(-1, HKV, D).index_copy_(0, sl, x[:, HQ + HKV:])
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(device)
+        return e0.elapsed_time(e1) / reps / layers
+
+    ms_fused = timed(fused)
+    mi.check_device_status(device)
+    ms_eager = timed(eager)
+    peaks, src = _peaks()
+    nbytes = prologue_bytes(tokens)
+    gbs = nbytes / (ms_fused * 1e-3) / 1e9
+    del pool, qkv, q_out
+    return {"workload": f"Qwen3-0.6B attention prologue, {tokens} tokens (BASELINE configs[3] "
+                        "prefill batch), bf16, split-half RoPE",
+            "kernel": "qk_prologue_kernel (RMSNorm q/k + RoPE + k/v store, one launch)",
+            "us_per_layer": round(ms_fused * 1e3, 2), "bytes_per_launch": nbytes,
+            "gbs": round(gbs, 1), "hbm_frac": round(gbs / peaks["hbm_gbs"], 4),
+            "peak_source": f"hbm_gbs of {src}",
+            "torch_eager_us_per_layer": round(ms_eager * 1e3, 2),
+            "speedup_vs_eager": round(ms_eager / ms_fused, 2)}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -880,7 +979,8 @@ def run_ours(args):
             line["extra"] = {"long_context_b1": measure_long_b1(device),
                              "long_context_batch256": measure_long_batch(device),
                              "prefill_mixed": measure_prefill(device, "mixed"),
-                             "prefill_shared_prefix": measure_prefill(device, "prefix")}
+                             "prefill_shared_prefix": measure_prefill(device, "prefix"),
+                             "attention_prologue": measure_prologue(device)}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)
@@ -928,6 +1028,22 @@ def run_profile(args):
 
         print(json.dumps({"profile": "long", "kernel": kernel, "split_k": split,
                           "decode_bytes_per_launch": decode_bytes([ctx_len], hq, hkv, D, 2, BS)}))
+        return
+    if args.profile == "prologue":
+        g = torch.Generator(device=device).manual_seed(21)
+        layers, tokens = 2, 8192
+        pool, qkv, qw, kw, cos, sin, positions, slots = _prologue_inputs(device, layers, tokens,
+                                                                         g)
+        for _ in range(args.steps):
+            for i in range(layers):
+                view = pool.layer(i)
+                mi.qk_norm_rope_store(qkv[i], qw[i], kw[i], positions, cos, sin, view.keys,
+                                      view.values, slots, num_q_heads=HQ, num_kv_heads=HKV,
+                                      eps=1e-6)
+        torch.cuda.synchronize(device)
+        mi.check_device_status(device)
+        print(json.dumps({"profile": "prologue", "layers": layers, "iterations": args.steps,
+                          "bytes_per_launch": prologue_bytes(tokens)}))
         return
     if args.profile in ("prefill", "mixed"):
         workload = "prefix" if args.profile == "prefill" else "mixed"
@@ -983,7 +1099,7 @@ def main():
                     help="reference = the reference's CPU path (oracle port); reference-gpu = "
                          "its Triton kernels on this GPU (needs baseline/_ref)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["decode", "long", "prefill", "mixed"], default=None,
+    ap.add_argument("--profile", choices=["decode", "long", "prefill", "mixed", "prologue"], default=None,
                     help="run a small eager case for ncu instead of the benchmark")
     ap.add_argument("--split-k", type=int, default=0)
     args = ap.parse_args()

@@ -62,6 +62,7 @@ extern "C" {
 #define MI_DEV_BAD_BLOCK 1 /* block id outside [0, num_blocks)     */
 #define MI_DEV_BAD_SLOT 2  /* slot outside [-1, num_blocks*bs)      */
 #define MI_DEV_TIMEOUT 4   /* a bounded mbarrier/flag wait ran out  */
+#define MI_DEV_BAD_POSITION 8 /* rotary position outside the cos/sin table */
 
 /* Version of this ABI (MI_ABI_VERSION). */
 MI_API int mi_abi_version(void);
@@ -88,6 +89,36 @@ MI_API int mi_store_kv(void *key_cache, void *value_cache, int64_t num_blocks,
                 int32_t index_dtype, const void *keys, const void *values,
                 int64_t key_token_stride, int64_t value_token_stride,
                 int64_t num_tokens, int32_t *dev_status, void *stream);
+
+/*
+ * Attention prologue in one launch: per-head RMSNorm of q and k
+ * (y = x / sqrt(mean(x^2) + eps) * weight, fp32, one rounding), rotary
+ * position embedding of q and k (split-half, or interleaved when
+ * `interleaved` != 0) with the caller's fp32 cos/sin tables
+ * [max_positions, head_dim / 2] indexed by positions[t], then k and v stored
+ * to slot_mapping[t] (-1 stores nothing) of the pool and q written to q_out.
+ * Replaces, before paged attention, q_norm / k_norm and RotaryCache.apply on
+ * q and k (microinfer/layer/transformer.py:222-225, layer/norm.py,
+ * layer/rope.py:6-21) and the store of k/v (layer/cached_attention.py:76-85),
+ * with the reference's rounding points.  qkv is the packed projection
+ * output, rows of [num_q_heads + 2 * num_kv_heads, head_dim] `qkv_token_stride`
+ * elements apart; q_out rows are [num_q_heads, head_dim], `q_out_token_stride`
+ * apart.  head_dim 64 or 128; dtype f32/f16/bf16 (weights in the same
+ * dtype); positions int32 or int64 (MI_INDEX_*).  Pointers and token strides
+ * must be 16-byte aligned.  Slots outside the pool are skipped
+ * (MI_DEV_BAD_SLOT), positions outside the table give zero rows
+ * (MI_DEV_BAD_POSITION).
+ */
+MI_API int mi_qk_norm_rope_store(void *q_out, int64_t q_out_token_stride, const void *qkv,
+                          int64_t qkv_token_stride, const void *q_weight,
+                          const void *k_weight, float eps, const void *positions,
+                          int32_t positions_dtype, const float *cos_table,
+                          const float *sin_table, int64_t max_positions,
+                          int32_t interleaved, const int32_t *slot_mapping,
+                          void *key_cache, void *value_cache, int64_t num_blocks,
+                          int32_t block_size, int64_t num_tokens, int32_t num_q_heads,
+                          int32_t num_kv_heads, int32_t head_dim, int32_t dtype,
+                          int32_t *dev_status, void *stream);
 
 /*
  * store_kvcache from flat slot ids (block * block_size + offset), splitting

@@ -13,6 +13,7 @@ reference's attention-backend interface:
 * ``worker.block_manager.CowBlockManager``           - refcounted pages, shared partial
   blocks and the (src, dst) copies that ``copy_blocks`` issues
 * ``layer.paged_attention.paged_attention_meta``     - backend dispatch
+* ``layer.prologue.qk_norm_rope_store``             - q/k RMSNorm + RoPE + k/v store
 
 ``install()`` rebinds a live ``microinfer`` import onto these entry points.
 """
@@ -30,6 +31,7 @@ from microinfer_b200.layer.paged_attention import (
     select_split_k,
     varlen_prefill,
 )
+from microinfer_b200.layer.prologue import qk_norm_rope_store
 from microinfer_b200.worker.block_manager import CowBlockManager, apply_copies
 from microinfer_b200.worker.kv_cache import KVCache, LayerKVCache, copy_blocks
 from microinfer_b200.worker.kv_store import store_kv, store_kv_slots
@@ -50,6 +52,7 @@ __all__ = [
     "paged_decode",
     "paged_decode_store",
     "paged_prefill",
+    "qk_norm_rope_store",
     "read_device_status",
     "select_split_k",
     "store_kv",

@@ -24,6 +24,7 @@ cudaError_t launch_attn_generic(const AttnParams &p, int dtype, bool paged, cuda
 bool decode_fast_supported(int dtype, int D, int G);
 bool decode_tc_supported(int dtype, int D, int G, int block_size);
 bool decode_mma_supported(int dtype, int D, int G, int block_size);
+cudaError_t launch_qk_prologue(const QkPrologueParams &p, int dtype, int D, cudaStream_t stream);
 cudaError_t launch_decode_mma(const DecodeParams &d, int dtype, int D, int G, int64_t num_seqs,
                               int nsplit, cudaStream_t stream);
 cudaError_t launch_decode_tc(const DecodeParams &d, int dtype, int G, int64_t num_seqs,
@@ -200,6 +201,60 @@ int mi_store_kv_slots(void *key_cache, void *value_cache, int64_t num_blocks, in
   return store_common(key_cache, value_cache, num_blocks, block_size, num_kv_heads, head_dim, dtype,
                       slots, nullptr, index_dtype, keys, values, key_token_stride,
                       value_token_stride, num_tokens, dev_status, stream, true);
+}
+
+int mi_qk_norm_rope_store(void *q_out, int64_t q_out_token_stride, const void *qkv,
+                          int64_t qkv_token_stride, const void *q_weight, const void *k_weight,
+                          float eps, const void *positions, int32_t positions_dtype,
+                          const float *cos_table, const float *sin_table, int64_t max_positions,
+                          int32_t interleaved, const int32_t *slot_mapping, void *key_cache,
+                          void *value_cache, int64_t num_blocks, int32_t block_size,
+                          int64_t num_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                          int32_t head_dim, int32_t dtype, int32_t *dev_status, void *stream) {
+  const int e = elem_size(dtype);
+  if (e == 0) return fail(MI_ERR_INVALID, "unknown dtype");
+  if (num_tokens < 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 ||
+      num_blocks <= 0 || block_size <= 0)
+    return fail(MI_ERR_INVALID, "sizes must be positive (num_tokens >= 0)");
+  if (head_dim != 64 && head_dim != 128) return fail(MI_ERR_UNSUPPORTED, "head_dim must be 64 or 128");
+  if (positions_dtype != MI_INDEX_INT32 && positions_dtype != MI_INDEX_INT64)
+    return fail(MI_ERR_INVALID, "positions must be int32 or int64");
+  if (!(eps >= 0.f)) return fail(MI_ERR_INVALID, "eps must be >= 0");
+  if (num_tokens == 0) return MI_OK;
+  if (!q_out || !qkv || !q_weight || !k_weight || !positions || !cos_table || !sin_table ||
+      !slot_mapping || !key_cache || !value_cache)
+    return fail(MI_ERR_INVALID, "null pointer");
+  if (max_positions <= 0) return fail(MI_ERR_INVALID, "max_positions must be positive");
+  const int64_t heads = num_q_heads + 2 * static_cast<int64_t>(num_kv_heads);
+  if (qkv_token_stride < heads * head_dim || q_out_token_stride < num_q_heads * int64_t{head_dim})
+    return fail(MI_ERR_INVALID, "token stride shorter than a row");
+  if (!aligned16(q_out) || !aligned16(qkv) || !aligned16(key_cache) || !aligned16(value_cache) ||
+      (qkv_token_stride * e) % 16 != 0 || (q_out_token_stride * e) % 16 != 0)
+    return fail(MI_ERR_ALIGNMENT, "pointers and token strides must be 16-byte aligned");
+  if (const int s = select_device(key_cache)) return s;
+  QkPrologueParams p = {};
+  p.qkv = static_cast<const char *>(qkv);
+  p.qkv_stride_bytes = qkv_token_stride * e;
+  p.q_weight = q_weight;
+  p.k_weight = k_weight;
+  p.eps = eps;
+  p.positions = positions;
+  p.positions_int64 = positions_dtype == MI_INDEX_INT64 ? 1 : 0;
+  p.cos_table = cos_table;
+  p.sin_table = sin_table;
+  p.max_positions = max_positions;
+  p.interleaved = interleaved ? 1 : 0;
+  p.slot_mapping = slot_mapping;
+  p.key_cache = static_cast<char *>(key_cache);
+  p.value_cache = static_cast<char *>(value_cache);
+  p.num_slots = num_blocks * block_size;
+  p.q_out = static_cast<char *>(q_out);
+  p.q_out_stride_bytes = q_out_token_stride * e;
+  p.num_tokens = num_tokens;
+  p.num_q_heads = num_q_heads;
+  p.num_kv_heads = num_kv_heads;
+  p.status = dev_status;
+  return cuda_status(launch_qk_prologue(p, dtype, head_dim, static_cast<cudaStream_t>(stream)));
 }
 
 size_t mi_paged_decode_workspace_bytes(int64_t num_seqs, int32_t num_q_heads, int32_t head_dim,

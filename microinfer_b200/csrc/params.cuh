@@ -98,4 +98,29 @@ struct DecodeParams {
   int32_t early_kv;
 };
 
+// Attention prologue (qk_prologue.cu): q/k RMSNorm + RoPE, k/v store.
+struct QkPrologueParams {
+  const char *qkv;  // [T, (Hq + 2 Hkv) * D] rows qkv_stride_bytes apart
+  int64_t qkv_stride_bytes;
+  const void *q_weight;  // [D] activation dtype
+  const void *k_weight;
+  float eps;
+  const void *positions;  // [T] int32 or int64
+  int32_t positions_int64;
+  const float *cos_table;  // [max_positions, D/2]
+  const float *sin_table;
+  int64_t max_positions;
+  int32_t interleaved;
+  const int32_t *slot_mapping;  // [T], -1: no store
+  char *key_cache;              // [num_slots, Hkv, D]
+  char *value_cache;
+  int64_t num_slots;
+  char *q_out;  // [T, Hq, D] rows q_out_stride_bytes apart
+  int64_t q_out_stride_bytes;
+  int64_t num_tokens;
+  int32_t num_q_heads;
+  int32_t num_kv_heads;
+  int32_t *status;
+};
+
 }  // namespace mi

@@ -212,6 +212,43 @@ def copy_blocks(key_pool, value_pool, pairs) -> None:
     value_pool[:, dst] = value_pool[:, src].copy()
 
 
+def qk_norm_rope(qkv, q_weight, k_weight, positions, cos_table, sin_table, *, num_q_heads,
+                 num_kv_heads, head_dim, eps, interleaved, dtype):
+    """Attention prologue: per-head RMSNorm of q and k, then RoPE; returns (q, k, v).
+
+    Follows Attention.forward (microinfer/layer/transformer.py:222-225): q_norm /
+    k_norm are F.rms_norm (layer/norm.py: fp32 ``x * rsqrt(mean(x^2) + eps) * w``,
+    one rounding to the activation dtype), then RotaryCache.apply
+    (layer/rope.py:6-21, 75-84): the rounded values widened to fp32, rotated
+    split-half (``cat(a*c - b*s, b*c + a*s)``) or interleaved
+    (``stack(a*c - b*s, a*s + b*c)``) with separately rounded fp32 products and
+    sums, rounded once more.  ``qkv`` is [T, (Hq + 2 Hkv) * D] in ``dtype``
+    (raw bits for bf16), the tables fp32 [max_positions, D/2].
+    """
+    d = head_dim
+    x = to_f32(np.asarray(qkv), dtype).reshape(len(qkv), num_q_heads + 2 * num_kv_heads, d)
+    q = x[:, :num_q_heads]
+    k = x[:, num_q_heads:num_q_heads + num_kv_heads]
+    v = x[:, num_q_heads + num_kv_heads:]
+    pos = np.asarray(positions, dtype=np.int64)
+    cos = np.asarray(cos_table, np.float32)[pos][:, None, :]
+    sin = np.asarray(sin_table, np.float32)[pos][:, None, :]
+
+    def norm_rope(h, w):
+        ms = np.mean(h * h, axis=-1, keepdims=True, dtype=np.float32)
+        inv = (np.float32(1) / np.sqrt(ms + np.float32(eps))).astype(np.float32)
+        y = to_f32(from_f32(h * inv * to_f32(np.asarray(w), dtype), dtype), dtype)
+        if interleaved:
+            a, b = y[..., 0::2], y[..., 1::2]
+            out = np.stack((a * cos - b * sin, a * sin + b * cos), axis=-1).reshape(y.shape)
+        else:
+            a, b = y[..., : d // 2], y[..., d // 2:]
+            out = np.concatenate((a * cos - b * sin, b * cos + a * sin), axis=-1)
+        return from_f32(out.astype(np.float32), dtype)
+
+    return norm_rope(q, q_weight), norm_rope(k, k_weight), from_f32(v, dtype)
+
+
 # ---------------------------------------------------------------------------
 # roofline accounting (algorithmic bytes / flops per launch)
 # ---------------------------------------------------------------------------
