@@ -530,6 +530,73 @@ def measure_prologue(device, tokens: int = 8192, layers: int = 8, reps: int = 20
             "speedup_vs_eager": round(ms_eager / ms_fused, 2)}
 
 
+def measure_runner_metadata(device, reps: int = 200):
+    """Per-step decode metadata: the device builder (worker/runner_metadata.py:
+    changed page-table entries + one 6-int record per sequence, one copy, one
+    launch) against the reference runner's host assembly restated
+    (oracle/runner_oracle.StagedDecodeRows: host loop over sequences and whole
+    block tables, five copies).  Each call is timed until its tensors are on the
+    device (synchronize after it).  Contexts U[128, 512] as BASELINE configs[1],
+    and a long-context batch (U[4K, 32K]) where whole tables are long."""
+    import numpy as np
+    import torch
+
+    import microinfer_b200 as mi
+    from oracle.runner_oracle import StagedDecodeRows
+
+    class _Seq:
+        def __init__(self, sid, n, table):
+            self.seq_id, self.num_tokens, self.block_table = sid, n, table
+            self.last_token, self.num_cached_tokens, self.num_scheduled_tokens = 1, n - 1, 1
+
+        def __len__(self):
+            return self.num_tokens
+
+    res = {}
+    for label, batch, lo, hi in (("b8_ctx128-512", 8, 128, 512), ("b64_ctx128-512", 64, 128, 512),
+                                 ("b256_ctx128-512", 256, 128, 512),
+                                 ("b64_ctx4k-32k", 64, 4096, 32768)):
+        rng = np.random.default_rng(batch)
+        grow = 2 * (reps + 3) // BS + 3  # pages each sequence gains over both timings
+        nb = batch * (hi // BS + 2 + grow) + 16
+        perm = rng.permutation(nb).tolist()
+        seqs = []
+        for i in range(batch):
+            n = int(rng.integers(lo, hi))
+            pages = (n + BS - 1) // BS + 1
+            seqs.append(_Seq(i, n, [perm.pop() for _ in range(pages)]))
+        width = max(len(s.block_table) for s in seqs) + grow
+        ours = mi.DeviceRunnerMetadata(BS, nb, max_rows=batch, max_pages=width, device=device)
+        base = StagedDecodeRows(BS, batch, width, device)
+
+        def advance():
+            for s in seqs:
+                s.num_tokens += 1
+                if (s.num_tokens - 1) // BS >= len(s.block_table):
+                    s.block_table.append(perm.pop())
+
+        def timed(fn):
+            times = []
+            for k in range(reps + 3):
+                t0 = time.perf_counter()
+                fn(seqs)
+                torch.cuda.synchronize(device)
+                if k >= 3:
+                    times.append(time.perf_counter() - t0)
+                advance()
+            return statistics.median(times) * 1e6
+
+        ours_us = timed(ours.prepare_decode)
+        mi.check_device_status(device)
+        base_us = timed(base.prepare_decode)
+        res[label] = {"device_builder_us": round(ours_us, 1),
+                      "host_assembly_us": round(base_us, 1),
+                      "speedup": round(base_us / ours_us, 2)}
+    return {"what": "decode metadata ready on the device, per step (median wall time incl. "
+                    "synchronize); device builder vs the reference runner's host assembly "
+                    "restated", "rows": res}
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -980,7 +1047,8 @@ def run_ours(args):
                              "long_context_batch256": measure_long_batch(device),
                              "prefill_mixed": measure_prefill(device, "mixed"),
                              "prefill_shared_prefix": measure_prefill(device, "prefix"),
-                             "attention_prologue": measure_prologue(device)}
+                             "attention_prologue": measure_prologue(device),
+                             "runner_metadata": measure_runner_metadata(device)}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line), flush=True)

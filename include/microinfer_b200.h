@@ -63,6 +63,7 @@ extern "C" {
 #define MI_DEV_BAD_SLOT 2  /* slot outside [-1, num_blocks*bs)      */
 #define MI_DEV_TIMEOUT 4   /* a bounded mbarrier/flag wait ran out  */
 #define MI_DEV_BAD_POSITION 8 /* rotary position outside the cos/sin table */
+#define MI_DEV_BAD_ROW 16     /* runner record: row, page count or range invalid */
 
 /* Version of this ABI (MI_ABI_VERSION). */
 MI_API int mi_abi_version(void);
@@ -89,6 +90,44 @@ MI_API int mi_store_kv(void *key_cache, void *value_cache, int64_t num_blocks,
                 int32_t index_dtype, const void *keys, const void *values,
                 int64_t key_token_stride, int64_t value_token_stride,
                 int64_t num_tokens, int32_t *dev_status, void *stream);
+
+/*
+ * Per-step runner metadata from a device-resident page table
+ * `page_table` [max_rows, max_pages] int32 (one row per running sequence,
+ * entries past a row's page count are ignored).  Replaces the reference
+ * runner's host-side assembly (microinfer/runner.py:160-188 _fill_decode_rows,
+ * :348-384 prepare_decode, :298-346 prepare_block_tables / prepare_prefill):
+ * the host sends `records` (int32 x 6 per sequence, in batch order) and only
+ * the page-table entries that changed, `updates` (int32 x 2: column, page id);
+ * one launch writes them into the table and produces the metadata tensors.
+ * Rows must be distinct within a call.  Records:
+ *   decode : row, num_tokens, last_token, num_pages, update_begin, update_count
+ *   prefill: row, start, end, num_pages, update_begin, update_count
+ * (update_begin/count index `updates`).  Decode writes, per sequence,
+ * input_ids = last_token, positions = num_tokens - 1, its slot, context_lens
+ * = num_tokens and the -1 padded block-table row [table_width]; prefill
+ * writes, per scheduled token (positions start..end-1, `token_ids` holding
+ * the scheduled tokens of all sequences concatenated), the id, position and
+ * slot, plus cu_seqlens_q/k [num_seqs + 1] and, when table_width > 0, the
+ * block tables.  Invalid records are flagged MI_DEV_BAD_ROW, invalid pages
+ * MI_DEV_BAD_BLOCK (slot -1).  All buffers are device memory.
+ */
+MI_API int mi_build_decode_metadata(int32_t *page_table, int32_t max_rows, int32_t max_pages,
+                                    const int32_t *records, int32_t num_seqs,
+                                    const int32_t *updates, int32_t num_updates,
+                                    int32_t block_size, int64_t num_blocks, int32_t table_width,
+                                    int64_t *input_ids, int64_t *positions, int32_t *slot_mapping,
+                                    int32_t *context_lens, int32_t *block_tables,
+                                    int32_t *dev_status, void *stream);
+MI_API int mi_build_prefill_metadata(int32_t *page_table, int32_t max_rows, int32_t max_pages,
+                                     const int32_t *records, int32_t num_seqs,
+                                     const int32_t *updates, int32_t num_updates,
+                                     const int32_t *token_ids, int64_t num_tokens,
+                                     int32_t block_size, int64_t num_blocks, int32_t table_width,
+                                     int64_t *input_ids, int64_t *positions,
+                                     int32_t *slot_mapping, int32_t *cu_seqlens_q,
+                                     int32_t *cu_seqlens_k, int32_t *block_tables,
+                                     int32_t *dev_status, void *stream);
 
 /*
  * Attention prologue in one launch: per-head RMSNorm of q and k

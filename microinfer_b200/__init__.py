@@ -14,6 +14,7 @@ reference's attention-backend interface:
   blocks and the (src, dst) copies that ``copy_blocks`` issues
 * ``layer.paged_attention.paged_attention_meta``     - backend dispatch
 * ``layer.prologue.qk_norm_rope_store``             - q/k RMSNorm + RoPE + k/v store
+* ``worker.runner_metadata.DeviceRunnerMetadata``  - per-step metadata from a device page table
 
 ``install()`` rebinds a live ``microinfer`` import onto these entry points.
 """
@@ -32,6 +33,7 @@ from microinfer_b200.layer.paged_attention import (
     varlen_prefill,
 )
 from microinfer_b200.layer.prologue import qk_norm_rope_store
+from microinfer_b200.worker.runner_metadata import DeviceRunnerMetadata
 from microinfer_b200.worker.block_manager import CowBlockManager, apply_copies
 from microinfer_b200.worker.kv_cache import KVCache, LayerKVCache, copy_blocks
 from microinfer_b200.worker.kv_store import store_kv, store_kv_slots
@@ -53,6 +55,7 @@ __all__ = [
     "paged_decode_store",
     "paged_prefill",
     "qk_norm_rope_store",
+    "DeviceRunnerMetadata",
     "read_device_status",
     "select_split_k",
     "store_kv",

@@ -23,6 +23,7 @@ DEV_BAD_BLOCK = 1
 DEV_BAD_SLOT = 2
 DEV_TIMEOUT = 4
 DEV_BAD_POSITION = 8
+DEV_BAD_ROW = 16
 
 _P = ctypes.c_void_p
 _I32 = ctypes.c_int32
@@ -83,6 +84,15 @@ SIGNATURES = {
     ),
     "mi_copy_blocks": (ctypes.c_int, [_P, _P, _I32, _I64, _I64, _I64, _P, _I64, _P, _P]),
     "mi_wait_flag_selftest": (ctypes.c_int, [_P, _I64, _P, _P]),
+    "mi_build_decode_metadata": (
+        ctypes.c_int,
+        [_P, _I32, _I32, _P, _I32, _P, _I32, _I32, _I64, _I32, _P, _P, _P, _P, _P, _P, _P],
+    ),
+    "mi_build_prefill_metadata": (
+        ctypes.c_int,
+        [_P, _I32, _I32, _P, _I32, _P, _I32, _P, _I64, _I32, _I64, _I32, _P, _P, _P, _P, _P, _P,
+         _P, _P],
+    ),
     "mi_qk_norm_rope_store": (
         ctypes.c_int,
         [_P, _I64, _P, _I64, _P, _P, _F, _P, _I32, _P, _P, _I64, _I32, _P, _P, _P, _I64, _I32,

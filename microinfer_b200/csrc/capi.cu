@@ -25,6 +25,8 @@ bool decode_fast_supported(int dtype, int D, int G);
 bool decode_tc_supported(int dtype, int D, int G, int block_size);
 bool decode_mma_supported(int dtype, int D, int G, int block_size);
 cudaError_t launch_qk_prologue(const QkPrologueParams &p, int dtype, int D, cudaStream_t stream);
+cudaError_t launch_decode_meta(const RunnerMetaParams &p, cudaStream_t stream);
+cudaError_t launch_prefill_meta(const RunnerMetaParams &p, cudaStream_t stream);
 cudaError_t launch_decode_mma(const DecodeParams &d, int dtype, int D, int G, int64_t num_seqs,
                               int nsplit, cudaStream_t stream);
 cudaError_t launch_decode_tc(const DecodeParams &d, int dtype, int G, int64_t num_seqs,
@@ -229,7 +231,8 @@ int mi_qk_norm_rope_store(void *q_out, int64_t q_out_token_stride, const void *q
   if (qkv_token_stride < heads * head_dim || q_out_token_stride < num_q_heads * int64_t{head_dim})
     return fail(MI_ERR_INVALID, "token stride shorter than a row");
   if (!aligned16(q_out) || !aligned16(qkv) || !aligned16(key_cache) || !aligned16(value_cache) ||
-      (qkv_token_stride * e) % 16 != 0 || (q_out_token_stride * e) % 16 != 0)
+      !aligned16(q_weight) || !aligned16(k_weight) || !aligned16(cos_table) ||
+      !aligned16(sin_table) || (qkv_token_stride * e) % 16 != 0 || (q_out_token_stride * e) % 16 != 0)
     return fail(MI_ERR_ALIGNMENT, "pointers and token strides must be 16-byte aligned");
   if (const int s = select_device(key_cache)) return s;
   QkPrologueParams p = {};
@@ -255,6 +258,96 @@ int mi_qk_norm_rope_store(void *q_out, int64_t q_out_token_stride, const void *q
   p.num_kv_heads = num_kv_heads;
   p.status = dev_status;
   return cuda_status(launch_qk_prologue(p, dtype, head_dim, static_cast<cudaStream_t>(stream)));
+}
+
+static int check_runner_meta(const int32_t *page_table, int32_t max_rows, int32_t max_pages,
+                             const int32_t *records, int32_t num_seqs, const int32_t *updates,
+                             int32_t num_updates, int32_t block_size, int64_t num_blocks,
+                             int32_t table_width) {
+  if (max_rows <= 0 || max_pages <= 0 || num_seqs < 0 || num_updates < 0 || block_size <= 0 ||
+      num_blocks <= 0 || table_width < 0 || table_width > max_pages)
+    return fail(MI_ERR_INVALID, "bad page-table or batch sizes");
+  if (num_blocks * static_cast<int64_t>(block_size) > INT32_MAX)
+    return fail(MI_ERR_INVALID, "slots must fit int32");
+  if (num_seqs > 0 && (!page_table || !records)) return fail(MI_ERR_INVALID, "null pointer");
+  if (num_updates > 0 && !updates) return fail(MI_ERR_INVALID, "null updates");
+  return MI_OK;
+}
+
+static RunnerMetaParams runner_meta_params(int32_t *page_table, int32_t max_rows, int32_t max_pages,
+                                           const int32_t *records, int32_t num_seqs,
+                                           const int32_t *updates, int32_t num_updates,
+                                           int32_t block_size, int64_t num_blocks,
+                                           int32_t table_width, int32_t *dev_status) {
+  RunnerMetaParams p = {};
+  p.page_table = page_table;
+  p.max_rows = max_rows;
+  p.max_pages = max_pages;
+  p.records = records;
+  p.num_seqs = num_seqs;
+  p.updates = updates;
+  p.num_updates = num_updates;
+  p.block_size = block_size;
+  p.num_blocks = num_blocks;
+  p.table_width = table_width;
+  p.status = dev_status;
+  return p;
+}
+
+int mi_build_decode_metadata(int32_t *page_table, int32_t max_rows, int32_t max_pages,
+                             const int32_t *records, int32_t num_seqs, const int32_t *updates,
+                             int32_t num_updates, int32_t block_size, int64_t num_blocks,
+                             int32_t table_width, int64_t *input_ids, int64_t *positions,
+                             int32_t *slot_mapping, int32_t *context_lens, int32_t *block_tables,
+                             int32_t *dev_status, void *stream) {
+  if (const int s = check_runner_meta(page_table, max_rows, max_pages, records, num_seqs, updates,
+                                      num_updates, block_size, num_blocks, table_width))
+    return s;
+  if (num_seqs == 0) return MI_OK;
+  if (!input_ids || !positions || !slot_mapping || !context_lens ||
+      (table_width > 0 && !block_tables))
+    return fail(MI_ERR_INVALID, "null output");
+  if (const int s = select_device(page_table)) return s;
+  RunnerMetaParams p = runner_meta_params(page_table, max_rows, max_pages, records, num_seqs,
+                                          updates, num_updates, block_size, num_blocks,
+                                          table_width, dev_status);
+  p.input_ids = input_ids;
+  p.positions = positions;
+  p.slot_mapping = slot_mapping;
+  p.context_lens = context_lens;
+  p.block_tables = block_tables;
+  return cuda_status(launch_decode_meta(p, static_cast<cudaStream_t>(stream)));
+}
+
+int mi_build_prefill_metadata(int32_t *page_table, int32_t max_rows, int32_t max_pages,
+                              const int32_t *records, int32_t num_seqs, const int32_t *updates,
+                              int32_t num_updates, const int32_t *token_ids, int64_t num_tokens,
+                              int32_t block_size, int64_t num_blocks, int32_t table_width,
+                              int64_t *input_ids, int64_t *positions, int32_t *slot_mapping,
+                              int32_t *cu_seqlens_q, int32_t *cu_seqlens_k,
+                              int32_t *block_tables, int32_t *dev_status, void *stream) {
+  if (const int s = check_runner_meta(page_table, max_rows, max_pages, records, num_seqs, updates,
+                                      num_updates, block_size, num_blocks, table_width))
+    return s;
+  if (num_tokens < 0 || num_tokens > INT32_MAX) return fail(MI_ERR_INVALID, "bad num_tokens");
+  if (num_seqs == 0) return MI_OK;
+  if (!cu_seqlens_q || !cu_seqlens_k || (num_tokens > 0 && (!token_ids || !input_ids ||
+                                                            !positions || !slot_mapping)) ||
+      (table_width > 0 && !block_tables))
+    return fail(MI_ERR_INVALID, "null pointer");
+  if (const int s = select_device(page_table)) return s;
+  RunnerMetaParams p = runner_meta_params(page_table, max_rows, max_pages, records, num_seqs,
+                                          updates, num_updates, block_size, num_blocks,
+                                          table_width, dev_status);
+  p.token_ids = token_ids;
+  p.num_tokens = num_tokens;
+  p.input_ids = input_ids;
+  p.positions = positions;
+  p.slot_mapping = slot_mapping;
+  p.cu_seqlens_q = cu_seqlens_q;
+  p.cu_seqlens_k = cu_seqlens_k;
+  p.block_tables = table_width > 0 ? block_tables : nullptr;
+  return cuda_status(launch_prefill_meta(p, static_cast<cudaStream_t>(stream)));
 }
 
 size_t mi_paged_decode_workspace_bytes(int64_t num_seqs, int32_t num_q_heads, int32_t head_dim,

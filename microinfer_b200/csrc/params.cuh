@@ -123,4 +123,28 @@ struct QkPrologueParams {
   int32_t *status;
 };
 
+// Per-step runner metadata from the device page table (runner_meta.cu).
+struct RunnerMetaParams {
+  int32_t *page_table;  // [max_rows, max_pages]
+  int32_t max_rows;
+  int32_t max_pages;
+  const int32_t *records;  // [num_seqs, 6]
+  int32_t num_seqs;
+  const int32_t *updates;  // [num_updates, 2]: column, page
+  int32_t num_updates;
+  const int32_t *token_ids;  // prefill: scheduled tokens, concatenated
+  int64_t num_tokens;
+  int32_t block_size;
+  int64_t num_blocks;
+  int32_t table_width;
+  int64_t *input_ids;
+  int64_t *positions;
+  int32_t *slot_mapping;
+  int32_t *context_lens;   // decode
+  int32_t *cu_seqlens_q;   // prefill
+  int32_t *cu_seqlens_k;   // prefill
+  int32_t *block_tables;   // [num_seqs, table_width], prefill: may be null
+  int32_t *status;
+};
+
 }  // namespace mi

@@ -18,10 +18,16 @@
 // The cos/sin tables are the caller's (the model's RotaryCache, fp32
 // [max_positions, D/2]); nothing here evaluates a trigonometric function.
 //
-// One warp per (token, head) of the packed qkv row [Hq | Hkv | Hkv] x D: lane
-// L holds elements [L*E, L*E + E) with E = D/32, so the split-half partner of
-// an element sits in lane L ^ 16 and the interleaved partner in the same lane.
-// HBM-bound: every element is read once and written once.
+// One CTA per token, 8 warps over the token's Hq + 2 Hkv head rows (up to 4
+// rows per warp per pass, all loaded before any is processed, so each warp
+// keeps 4 row loads in flight).  Lane L holds elements [L*E, L*E + E) with
+// E = D/32, so the split-half partner of an element sits in lane L ^ 16 and the
+// interleaved partner in the same lane.  Position, slot, the cos/sin
+// coefficients and the two weight vectors are read once per warp for all of
+// the token's heads.  Products and sums use the packed f32x2 instructions
+// with explicit round-to-nearest (each lane rounded exactly as __fmul_rn /
+// __fadd_rn; a negated operand turns a sum into the reference's difference
+// exactly).  HBM-bound: every element is read once and written once.
 #include <type_traits>
 
 #include "common.cuh"
@@ -32,109 +38,175 @@ namespace mi {
 
 namespace {
 
-constexpr int kPrologueWarps = 8;
+constexpr int kPrologueThreads = 256;
+constexpr int kPrologueWarps = kPrologueThreads / 32;
+constexpr int kRowsPerWarp = 4;
 
-// E consecutive elements of T as one aligned vector access.
+// E consecutive elements of T as one aligned vector.
 template <typename T, int E>
 struct RowVec {
   static constexpr int kBytes = E * static_cast<int>(sizeof(T));
   using V = typename std::conditional<kBytes == 16, uint4,
                                       typename std::conditional<kBytes == 8, uint2, uint32_t>::type>::type;
-  __device__ __forceinline__ static void load(const void *src, float (&x)[E]) {
-    const V v = *reinterpret_cast<const V *>(src);
+  static constexpr int kWords = kBytes / 4;
+  __device__ __forceinline__ static void to_float(const V &v, float (&x)[E]) {
     const T *e = reinterpret_cast<const T *>(&v);
 #pragma unroll
     for (int i = 0; i < E; ++i) x[i] = Elem<T>::to_float(e[i]);
   }
-  __device__ __forceinline__ static void store(void *dst, const float (&x)[E]) {
+  __device__ __forceinline__ static V from_float(const float (&x)[E]) {
     V v;
     T *e = reinterpret_cast<T *>(&v);
 #pragma unroll
     for (int i = 0; i < E; ++i) e[i] = Elem<T>::from_float(x[i]);
-    *reinterpret_cast<V *>(dst) = v;
+    return v;
   }
-  __device__ __forceinline__ static void copy(void *dst, const void *src) {
-    *reinterpret_cast<V *>(dst) = *reinterpret_cast<const V *>(src);
+  __device__ __forceinline__ static uint32_t word(const V &v, int i) {
+    return reinterpret_cast<const uint32_t *>(&v)[i];
+  }
+  __device__ __forceinline__ static void set_word(V &v, int i, uint32_t w) {
+    reinterpret_cast<uint32_t *>(&v)[i] = w;
   }
 };
+
+// n consecutive fp32 values as one vector load (n = 1, 2 or 4).
+template <int N>
+__device__ __forceinline__ void load_f32(const float *src, float (&dst)[N]) {
+  if constexpr (N == 4) {
+    const float4 v = *reinterpret_cast<const float4 *>(src);
+    dst[0] = v.x, dst[1] = v.y, dst[2] = v.z, dst[3] = v.w;
+  } else if constexpr (N == 2) {
+    const float2 v = *reinterpret_cast<const float2 *>(src);
+    dst[0] = v.x, dst[1] = v.y;
+  } else {
+    dst[0] = *src;
+  }
+}
 
 }  // namespace
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kPrologueWarps * 32) qk_prologue_kernel(const QkPrologueParams p) {
+__global__ void __launch_bounds__(kPrologueThreads, 4) qk_prologue_kernel(const QkPrologueParams p) {
   constexpr int E = D / 32;  // elements per lane
   using RV = RowVec<T, E>;
+  using V = typename RV::V;
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int heads = p.num_q_heads + 2 * p.num_kv_heads;
-  const int64_t item = static_cast<int64_t>(blockIdx.x) * kPrologueWarps + warp;
-  if (item < p.num_tokens * heads) {
-    const int64_t t = item / heads;
-    const int h = static_cast<int>(item - t * heads);
-    const int kind = h < p.num_q_heads ? 0 : (h < p.num_q_heads + p.num_kv_heads ? 1 : 2);
-    const char *src = p.qkv + t * p.qkv_stride_bytes + (static_cast<int64_t>(h) * D + lane * E) * sizeof(T);
-    int64_t slot = -1;
-    if (kind != 0) {
-      slot = p.slot_mapping[t];
-      if (slot < -1 || slot >= p.num_slots) {
-        if (lane == 0) flag_status(p.status, MI_DEV_BAD_SLOT);
-        slot = -1;
-      }
-    }
-    const int kvh = h - p.num_q_heads - (kind == 2 ? p.num_kv_heads : 0);
-    const int64_t cache_off = (slot * p.num_kv_heads + kvh) * D * static_cast<int64_t>(sizeof(T)) +
-                              lane * E * static_cast<int64_t>(sizeof(T));
-    if (kind == 2) {
-      if (slot >= 0) RV::copy(p.value_cache + cache_off, src);
+  const int64_t t = blockIdx.x;
+  const int hq = p.num_q_heads, hkv = p.num_kv_heads, heads = hq + 2 * hkv;
+
+  const int64_t pos = p.positions_int64 ? static_cast<const int64_t *>(p.positions)[t]
+                                        : static_cast<const int32_t *>(p.positions)[t];
+  const bool pos_ok = pos >= 0 && pos < p.max_positions;
+  int64_t slot = p.slot_mapping[t];
+  const bool slot_bad = slot < -1 || slot >= p.num_slots;
+  if (slot_bad) slot = -1;
+  if (threadIdx.x == 0) {
+    if (!pos_ok) flag_status(p.status, MI_DEV_BAD_POSITION);
+    if (slot_bad) flag_status(p.status, MI_DEV_BAD_SLOT);
+  }
+
+  // Rotation coefficients of this lane's elements (identical for every head).
+  float cs[E], sn[E];
+  if (pos_ok) {
+    if (p.interleaved) {
+      const int64_t off = pos * (D / 2) + lane * (E / 2);
+      float c2[E / 2], s2[E / 2];
+      load_f32<E / 2>(p.cos_table + off, c2);
+      load_f32<E / 2>(p.sin_table + off, s2);
+#pragma unroll
+      for (int j = 0; j < E / 2; ++j) cs[2 * j] = cs[2 * j + 1] = c2[j], sn[2 * j] = sn[2 * j + 1] = s2[j];
     } else {
+      const int64_t off = pos * (D / 2) + (lane & 15) * E;
+      load_f32<E>(p.cos_table + off, cs);
+      load_f32<E>(p.sin_table + off, sn);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < E; ++i) cs[i] = sn[i] = 0.f;  // unused: the rows are zeroed
+  }
+  float wq[E], wk[E];
+  RV::to_float(*reinterpret_cast<const V *>(static_cast<const T *>(p.q_weight) + lane * E), wq);
+  RV::to_float(*reinterpret_cast<const V *>(static_cast<const T *>(p.k_weight) + lane * E), wk);
+  const bool upper = lane >= 16;  // split-half: elements D/2 .. D-1
+
+  const char *row0 = p.qkv + t * p.qkv_stride_bytes + lane * E * static_cast<int64_t>(sizeof(T));
+  const int64_t lane_off = lane * E * static_cast<int64_t>(sizeof(T));
+  for (int base = warp; base < heads; base += kPrologueWarps * kRowsPerWarp) {
+    V raw[kRowsPerWarp];
+#pragma unroll
+    for (int j = 0; j < kRowsPerWarp; ++j) {
+      const int h = base + j * kPrologueWarps;
+      if (h < heads) raw[j] = *reinterpret_cast<const V *>(row0 + static_cast<int64_t>(h) * D * sizeof(T));
+    }
+#pragma unroll
+    for (int j = 0; j < kRowsPerWarp; ++j) {
+      const int h = base + j * kPrologueWarps;
+      if (h >= heads) break;  // warp-uniform
+      if (h >= hq + hkv) {    // v: raw copy into its slot
+        if (slot >= 0)
+          *reinterpret_cast<V *>(p.value_cache + (slot * hkv + (h - hq - hkv)) * D * static_cast<int64_t>(sizeof(T)) +
+                                 lane_off) = raw[j];
+        continue;
+      }
+      const bool is_q = h < hq;
       float x[E];
-      RV::load(src, x);
-      // RMSNorm (fp32, one rounding to T, as F.rms_norm)
+      RV::to_float(raw[j], x);
+      // RMSNorm: fp32, one rounding to T (F.rms_norm)
       float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < E; ++i) ss = fmaf(x[i], x[i], ss);
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
       const float inv = 1.f / sqrtf(ss / static_cast<float>(D) + p.eps);
-      const T *w = static_cast<const T *>(kind == 0 ? p.q_weight : p.k_weight) + lane * E;
       float y[E];
 #pragma unroll
-      for (int i = 0; i < E; ++i)
-        y[i] = Elem<T>::to_float(Elem<T>::from_float(__fmul_rn(__fmul_rn(x[i], inv), Elem<T>::to_float(w[i]))));
-      // RoPE on the rounded values
-      const int64_t pos = p.positions_int64 ? static_cast<const int64_t *>(p.positions)[t]
-                                            : static_cast<const int32_t *>(p.positions)[t];
+      for (int i = 0; i < E; i += 2) {
+        const float2 w2 = is_q ? make_float2(wq[i], wq[i + 1]) : make_float2(wk[i], wk[i + 1]);
+        const float2 v2 = fmul2(fmul2(make_float2(x[i], x[i + 1]), make_float2(inv, inv)), w2);
+        y[i] = v2.x, y[i + 1] = v2.y;
+      }
+      V yb = RV::from_float(y);  // the rounded norm output, as the reference holds it
+      RV::to_float(yb, y);
       float out[E];
-      if (pos < 0 || pos >= p.max_positions) {
-        if (lane == 0) flag_status(p.status, MI_DEV_BAD_POSITION);
+      if (p.interleaved) {
+        // out[2j] = a c - b s, out[2j+1] = a s + b c
 #pragma unroll
-        for (int i = 0; i < E; ++i) out[i] = 0.f;
-      } else if (p.interleaved) {
-        const float *cs = p.cos_table + pos * (D / 2) + lane * (E / 2);
-        const float *sn = p.sin_table + pos * (D / 2) + lane * (E / 2);
-#pragma unroll
-        for (int j = 0; j < E / 2; ++j) {
-          const float c = cs[j], s = sn[j], a = y[2 * j], b = y[2 * j + 1];
-          out[2 * j] = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-          out[2 * j + 1] = __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+        for (int i = 0; i < E; i += 2) {
+          const float2 m1 = fmul2(make_float2(y[i], y[i]), make_float2(cs[i], sn[i]));
+          const float2 m2 = fmul2(make_float2(y[i + 1], y[i + 1]), make_float2(sn[i], cs[i]));
+          const float2 o = fadd2(m1, make_float2(-m2.x, m2.y));
+          out[i] = o.x, out[i + 1] = o.y;
         }
       } else {
-        const bool upper = lane >= 16;  // elements D/2 .. D-1
-        const int j0 = (lane & 15) * E;
+        // partner element (i +- D/2) from lane ^ 16, moved as packed T words
+        V pb;
+#pragma unroll
+        for (int w = 0; w < RV::kWords; ++w)
+          RV::set_word(pb, w, __shfl_xor_sync(0xffffffffu, RV::word(yb, w), 16));
         float partner[E];
+        RV::to_float(pb, partner);
+        // lower: y c - partner s; upper: y c + partner s
 #pragma unroll
-        for (int i = 0; i < E; ++i) partner[i] = __shfl_xor_sync(0xffffffffu, y[i], 16);
-#pragma unroll
-        for (int i = 0; i < E; ++i) {
-          const float c = p.cos_table[pos * (D / 2) + j0 + i], s = p.sin_table[pos * (D / 2) + j0 + i];
-          out[i] = upper ? __fadd_rn(__fmul_rn(y[i], c), __fmul_rn(partner[i], s))
-                         : __fsub_rn(__fmul_rn(y[i], c), __fmul_rn(partner[i], s));
+        for (int i = 0; i < E; i += 2) {
+          const float2 m1 = fmul2(make_float2(y[i], y[i + 1]), make_float2(cs[i], cs[i + 1]));
+          float2 m2 = fmul2(make_float2(partner[i], partner[i + 1]), make_float2(sn[i], sn[i + 1]));
+          if (!upper) m2 = make_float2(-m2.x, -m2.y);
+          const float2 o = fadd2(m1, m2);
+          out[i] = o.x, out[i + 1] = o.y;
         }
       }
-      if (kind == 0)
-        RV::store(p.q_out + t * p.q_out_stride_bytes + (static_cast<int64_t>(h) * D + lane * E) * sizeof(T), out);
+      if (!pos_ok) {
+#pragma unroll
+        for (int i = 0; i < E; ++i) out[i] = 0.f;
+      }
+      const V ob = RV::from_float(out);
+      if (is_q)
+        *reinterpret_cast<V *>(p.q_out + t * p.q_out_stride_bytes + static_cast<int64_t>(h) * D * sizeof(T) +
+                               lane_off) = ob;
       else if (slot >= 0)
-        RV::store(p.key_cache + cache_off, out);
+        *reinterpret_cast<V *>(p.key_cache + (slot * hkv + (h - hq)) * D * static_cast<int64_t>(sizeof(T)) +
+                               lane_off) = ob;
     }
   }
   pdl_launch_dependents();
@@ -142,10 +214,8 @@ __global__ void __launch_bounds__(kPrologueWarps * 32) qk_prologue_kernel(const 
 
 template <typename T>
 static cudaError_t launch_prologue_t(const QkPrologueParams &p, int D, cudaStream_t stream) {
-  const int64_t items = p.num_tokens * (p.num_q_heads + 2 * p.num_kv_heads);
-  const int64_t blocks = (items + kPrologueWarps - 1) / kPrologueWarps;
-  if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
-  const dim3 grid(static_cast<unsigned>(blocks)), block(kPrologueWarps * 32);
+  if (p.num_tokens > 0x7fffffff) return cudaErrorInvalidValue;
+  const dim3 grid(static_cast<unsigned>(p.num_tokens)), block(kPrologueThreads);
   if (D == 128) return launch_pdl(qk_prologue_kernel<T, 128>, grid, block, 0, stream, p);
   return launch_pdl(qk_prologue_kernel<T, 64>, grid, block, 0, stream, p);
 }
