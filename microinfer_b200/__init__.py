@@ -37,6 +37,7 @@ from microinfer_b200.worker.runner_metadata import DeviceRunnerMetadata
 from microinfer_b200.worker.block_manager import CowBlockManager, apply_copies
 from microinfer_b200.worker.kv_cache import KVCache, LayerKVCache, copy_blocks
 from microinfer_b200.worker.kv_store import store_kv, store_kv_slots
+from microinfer_b200 import torch_ops  # noqa: E402,F401  (registers torch.ops.microinfer_b200.*)
 
 __all__ = [
     "AttentionMetadata",

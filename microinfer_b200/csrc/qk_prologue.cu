@@ -40,7 +40,7 @@ namespace {
 
 constexpr int kPrologueThreads = 256;
 constexpr int kPrologueWarps = kPrologueThreads / 32;
-constexpr int kRowsPerWarp = 4;
+constexpr int kRowsPerWarp = 2;  // row groups per warp loaded ahead
 
 // E consecutive elements of T as one aligned vector.
 template <typename T, int E>
@@ -50,9 +50,19 @@ struct RowVec {
                                       typename std::conditional<kBytes == 8, uint2, uint32_t>::type>::type;
   static constexpr int kWords = kBytes / 4;
   __device__ __forceinline__ static void to_float(const V &v, float (&x)[E]) {
-    const T *e = reinterpret_cast<const T *>(&v);
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      // exact widening by bit placement (plain ALU ops)
+      const uint32_t *w = reinterpret_cast<const uint32_t *>(&v);
 #pragma unroll
-    for (int i = 0; i < E; ++i) x[i] = Elem<T>::to_float(e[i]);
+      for (int i = 0; i < E / 2; ++i) {
+        x[2 * i] = __uint_as_float(w[i] << 16);
+        x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+      }
+    } else {
+      const T *e = reinterpret_cast<const T *>(&v);
+#pragma unroll
+      for (int i = 0; i < E; ++i) x[i] = Elem<T>::to_float(e[i]);
+    }
   }
   __device__ __forceinline__ static V from_float(const float (&x)[E]) {
     V v;
@@ -68,6 +78,42 @@ struct RowVec {
     reinterpret_cast<uint32_t *>(&v)[i] = w;
   }
 };
+
+// fp32 -> bf16 round-to-nearest-even with integer operations, the result left
+// in the upper half of an fp32 word (so it is also the widened bf16 value):
+// add 0x7fff plus the lowest kept bit, then clear the low half; a carry into the
+// exponent gives the correctly rounded overflow to infinity.  NaN stays a quiet
+// NaN.  The packed conversion instruction runs on the same pipe as the square
+// root and reciprocal and would bound this kernel; these are plain ALU ops.
+__device__ __forceinline__ uint32_t bf16_rne_bits(float f) {
+  const uint32_t u = __float_as_uint(f);
+  const uint32_t r = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
+  return f != f ? 0x7fc00000u : r;
+}
+
+// Round E fp32 values to T and return them packed; `y` receives the rounded
+// values widened back to fp32.
+template <typename T, int E, typename V>
+__device__ __forceinline__ V round_pack(const float (&x)[E], float (&y)[E]) {
+  V v;
+  uint32_t *w = reinterpret_cast<uint32_t *>(&v);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+#pragma unroll
+    for (int i = 0; i < E; i += 2) {
+      const uint32_t lo = bf16_rne_bits(x[i]), hi = bf16_rne_bits(x[i + 1]);
+      y[i] = __uint_as_float(lo), y[i + 1] = __uint_as_float(hi);
+      w[i / 2] = __byte_perm(lo, hi, 0x7632);  // upper halves: element i low, i+1 high
+    }
+  } else {
+    T *e = reinterpret_cast<T *>(&v);
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      e[i] = Elem<T>::from_float(x[i]);
+      y[i] = Elem<T>::to_float(e[i]);
+    }
+  }
+  return v;
+}
 
 // n consecutive fp32 values as one vector load (n = 1, 2 or 4).
 template <int N>
@@ -86,12 +132,17 @@ __device__ __forceinline__ void load_f32(const float *src, float (&dst)[N]) {
 }  // namespace
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kPrologueThreads, 4) qk_prologue_kernel(const QkPrologueParams p) {
-  constexpr int E = D / 32;  // elements per lane
+__global__ void __launch_bounds__(kPrologueThreads, 3) qk_prologue_kernel(const QkPrologueParams p) {
+  constexpr int E = 16 / static_cast<int>(sizeof(T));  // elements per lane: one 16-byte vector
+  constexpr int G = D / E;                             // lanes per head row
+  constexpr int R = 32 / G;                            // rows one warp instruction covers
+  constexpr int kPass = kRowsPerWarp;                  // row groups loaded before any is used
+  static_assert(G >= 2 && G <= 32 && 32 % G == 0, "a head row must span a power-of-two lane group");
   using RV = RowVec<T, E>;
   using V = typename RV::V;
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gl = lane & (G - 1), sub = lane / G;  // lane within its row, row within the warp
   const int64_t t = blockIdx.x;
   const int hq = p.num_q_heads, hkv = p.num_kv_heads, heads = hq + 2 * hkv;
 
@@ -106,68 +157,72 @@ __global__ void __launch_bounds__(kPrologueThreads, 4) qk_prologue_kernel(const 
     if (slot_bad) flag_status(p.status, MI_DEV_BAD_SLOT);
   }
 
-  // Rotation coefficients of this lane's elements (identical for every head).
+  // Rotation coefficients of this lane's elements (the same for every head).
   float cs[E], sn[E];
+#pragma unroll
+  for (int i = 0; i < E; ++i) cs[i] = sn[i] = 0.f;  // bad positions: rows are zeroed below
   if (pos_ok) {
     if (p.interleaved) {
-      const int64_t off = pos * (D / 2) + lane * (E / 2);
-      float c2[E / 2], s2[E / 2];
-      load_f32<E / 2>(p.cos_table + off, c2);
-      load_f32<E / 2>(p.sin_table + off, s2);
+      const int64_t off = pos * (D / 2) + gl * (E / 2);
 #pragma unroll
-      for (int j = 0; j < E / 2; ++j) cs[2 * j] = cs[2 * j + 1] = c2[j], sn[2 * j] = sn[2 * j + 1] = s2[j];
-    } else {
-      const int64_t off = pos * (D / 2) + (lane & 15) * E;
-      load_f32<E>(p.cos_table + off, cs);
-      load_f32<E>(p.sin_table + off, sn);
-    }
-  } else {
+      for (int j = 0; j < E / 2; j += 4) {
+        float c4[4], s4[4];
+        load_f32<(E / 2 < 4 ? E / 2 : 4)>(p.cos_table + off + j, reinterpret_cast<float(&)[(E / 2 < 4 ? E / 2 : 4)]>(c4));
+        load_f32<(E / 2 < 4 ? E / 2 : 4)>(p.sin_table + off + j, reinterpret_cast<float(&)[(E / 2 < 4 ? E / 2 : 4)]>(s4));
 #pragma unroll
-    for (int i = 0; i < E; ++i) cs[i] = sn[i] = 0.f;  // unused: the rows are zeroed
-  }
-  float wq[E], wk[E];
-  RV::to_float(*reinterpret_cast<const V *>(static_cast<const T *>(p.q_weight) + lane * E), wq);
-  RV::to_float(*reinterpret_cast<const V *>(static_cast<const T *>(p.k_weight) + lane * E), wk);
-  const bool upper = lane >= 16;  // split-half: elements D/2 .. D-1
-
-  const char *row0 = p.qkv + t * p.qkv_stride_bytes + lane * E * static_cast<int64_t>(sizeof(T));
-  const int64_t lane_off = lane * E * static_cast<int64_t>(sizeof(T));
-  for (int base = warp; base < heads; base += kPrologueWarps * kRowsPerWarp) {
-    V raw[kRowsPerWarp];
-#pragma unroll
-    for (int j = 0; j < kRowsPerWarp; ++j) {
-      const int h = base + j * kPrologueWarps;
-      if (h < heads) raw[j] = *reinterpret_cast<const V *>(row0 + static_cast<int64_t>(h) * D * sizeof(T));
-    }
-#pragma unroll
-    for (int j = 0; j < kRowsPerWarp; ++j) {
-      const int h = base + j * kPrologueWarps;
-      if (h >= heads) break;  // warp-uniform
-      if (h >= hq + hkv) {    // v: raw copy into its slot
-        if (slot >= 0)
-          *reinterpret_cast<V *>(p.value_cache + (slot * hkv + (h - hq - hkv)) * D * static_cast<int64_t>(sizeof(T)) +
-                                 lane_off) = raw[j];
-        continue;
+        for (int u = 0; u < (E / 2 < 4 ? E / 2 : 4); ++u)
+          cs[2 * (j + u)] = cs[2 * (j + u) + 1] = c4[u], sn[2 * (j + u)] = sn[2 * (j + u) + 1] = s4[u];
       }
-      const bool is_q = h < hq;
+    } else {
+      const int64_t off = pos * (D / 2) + (gl & (G / 2 - 1)) * E;
+#pragma unroll
+      for (int j = 0; j < E; j += 4) {
+        load_f32<4>(p.cos_table + off + j, reinterpret_cast<float(&)[4]>(cs[j]));
+        load_f32<4>(p.sin_table + off + j, reinterpret_cast<float(&)[4]>(sn[j]));
+      }
+    }
+  }
+  // Norm weights of this lane's elements, kept packed.
+  const V wq = *reinterpret_cast<const V *>(static_cast<const T *>(p.q_weight) + gl * E);
+  const V wk = *reinterpret_cast<const V *>(static_cast<const T *>(p.k_weight) + gl * E);
+  const bool upper = gl >= G / 2;  // split-half: elements D/2 .. D-1
+  const int64_t lane_off = gl * E * static_cast<int64_t>(sizeof(T));
+  const char *row0 = p.qkv + t * p.qkv_stride_bytes + lane_off;
+  constexpr int kStep = kPrologueWarps * R * kPass;  // rows per CTA pass
+
+  for (int base = 0; base < heads; base += kStep) {
+    V raw[kPass];
+#pragma unroll
+    for (int j = 0; j < kPass; ++j) {
+      const int h = base + (j * kPrologueWarps + warp) * R + sub;
+      raw[j] = h < heads ? *reinterpret_cast<const V *>(row0 + static_cast<int64_t>(h) * D * sizeof(T)) : V{};
+    }
+#pragma unroll
+    for (int j = 0; j < kPass; ++j) {
+      const int h0 = base + (j * kPrologueWarps + warp) * R;
+      if (h0 >= heads) break;  // warp-uniform
+      const int h = h0 + sub;
+      // every lane runs the q/k math (v and out-of-range lanes discard it), so the
+      // shuffles below see whole groups
       float x[E];
       RV::to_float(raw[j], x);
-      // RMSNorm: fp32, one rounding to T (F.rms_norm)
       float ss = 0.f;
 #pragma unroll
       for (int i = 0; i < E; ++i) ss = fmaf(x[i], x[i], ss);
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      for (int off = G / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
       const float inv = 1.f / sqrtf(ss / static_cast<float>(D) + p.eps);
+      float w[E];
+      RV::to_float(h < hq ? wq : wk, w);
+      // RMSNorm: fp32, one rounding to T (F.rms_norm)
       float y[E];
 #pragma unroll
       for (int i = 0; i < E; i += 2) {
-        const float2 w2 = is_q ? make_float2(wq[i], wq[i + 1]) : make_float2(wk[i], wk[i + 1]);
-        const float2 v2 = fmul2(fmul2(make_float2(x[i], x[i + 1]), make_float2(inv, inv)), w2);
+        const float2 v2 = fmul2(fmul2(make_float2(x[i], x[i + 1]), make_float2(inv, inv)),
+                                make_float2(w[i], w[i + 1]));
         y[i] = v2.x, y[i + 1] = v2.y;
       }
-      V yb = RV::from_float(y);  // the rounded norm output, as the reference holds it
-      RV::to_float(yb, y);
+      const V yb = round_pack<T, E, V>(y, y);  // the rounded norm output, as the reference holds it
       float out[E];
       if (p.interleaved) {
         // out[2j] = a c - b s, out[2j+1] = a s + b c
@@ -179,11 +234,11 @@ __global__ void __launch_bounds__(kPrologueThreads, 4) qk_prologue_kernel(const 
           out[i] = o.x, out[i + 1] = o.y;
         }
       } else {
-        // partner element (i +- D/2) from lane ^ 16, moved as packed T words
+        // partner elements (i +- D/2) from lane ^ G/2, moved as packed T words
         V pb;
 #pragma unroll
-        for (int w = 0; w < RV::kWords; ++w)
-          RV::set_word(pb, w, __shfl_xor_sync(0xffffffffu, RV::word(yb, w), 16));
+        for (int wd = 0; wd < RV::kWords; ++wd)
+          RV::set_word(pb, wd, __shfl_xor_sync(0xffffffffu, RV::word(yb, wd), G / 2));
         float partner[E];
         RV::to_float(pb, partner);
         // lower: y c - partner s; upper: y c + partner s
@@ -200,13 +255,18 @@ __global__ void __launch_bounds__(kPrologueThreads, 4) qk_prologue_kernel(const 
 #pragma unroll
         for (int i = 0; i < E; ++i) out[i] = 0.f;
       }
-      const V ob = RV::from_float(out);
-      if (is_q)
+      float unused[E];
+      const V ob = round_pack<T, E, V>(out, unused);
+      if (h < hq) {
         *reinterpret_cast<V *>(p.q_out + t * p.q_out_stride_bytes + static_cast<int64_t>(h) * D * sizeof(T) +
                                lane_off) = ob;
-      else if (slot >= 0)
-        *reinterpret_cast<V *>(p.key_cache + (slot * hkv + (h - hq)) * D * static_cast<int64_t>(sizeof(T)) +
-                               lane_off) = ob;
+      } else if (h < heads && slot >= 0) {
+        const bool is_k = h < hq + hkv;
+        char *cache = is_k ? p.key_cache : p.value_cache;
+        const int kvh = is_k ? h - hq : h - hq - hkv;
+        *reinterpret_cast<V *>(cache + (slot * hkv + kvh) * D * static_cast<int64_t>(sizeof(T)) + lane_off) =
+            is_k ? ob : raw[j];
+      }
     }
   }
   pdl_launch_dependents();

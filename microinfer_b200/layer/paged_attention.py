@@ -142,6 +142,10 @@ def paged_decode(query, key_cache, value_cache, block_tables, context_lens, *,
                  scale: float | None = None, split_k: int | None = None,
                  out: torch.Tensor | None = None) -> torch.Tensor:
     """One query token per request over its paged KV (any block size)."""
+    if torch.compiler.is_compiling():  # an opaque node for torch.compile
+        res = torch.ops.microinfer_b200.paged_decode(query, key_cache, value_cache, block_tables,
+                                                     context_lens, scale, split_k)
+        return res if out is None else out.copy_(res)
     if query.shape[0] == 0:
         return torch.empty_like(query)
     a = _decode_prep(query, key_cache, value_cache, block_tables, context_lens, split_k, scale, out)
@@ -169,6 +173,11 @@ def paged_decode_store(query, key_cache, value_cache, block_tables, context_lens
     launch); use it only when that kernel writes neither the pool nor the
     tables/lengths (a QKV projection, or another layer's decode).
     """
+    if torch.compiler.is_compiling():  # an opaque node for torch.compile
+        res = torch.ops.microinfer_b200.paged_decode_store(
+            query, key_cache, value_cache, block_tables, context_lens, k_new, v_new,
+            slot_mapping, scale, split_k, early_kv)
+        return res if out is None else out.copy_(res)
     if query.shape[0] == 0:
         return torch.empty_like(query)
     n = query.shape[0]
@@ -206,6 +215,11 @@ def paged_prefill(query, key_cache, value_cache, cu_seqlens_q, cu_seqlens_k, blo
     ``cu_seqlens_k`` is cumulative over contexts (context includes the chunk),
     so request r's rows sit at positions ``context_r - q_len_r + i``.
     """
+    if torch.compiler.is_compiling():  # an opaque node for torch.compile
+        res = torch.ops.microinfer_b200.paged_prefill(query, key_cache, value_cache, cu_seqlens_q,
+                                                      cu_seqlens_k, block_tables,
+                                                      int(max_seqlen_q), scale)
+        return res if out is None else out.copy_(res)
     num_q_heads, head_dim, block_size, num_kv_heads = _check_common(query, key_cache, value_cache)
     num_tokens = query.shape[0]
     num_requests = block_tables.shape[0]

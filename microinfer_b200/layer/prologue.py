@@ -28,6 +28,11 @@ def qk_norm_rope_store(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torc
     Hkv, D]) and return q as [T, Hq, D].  ``cos_table``/``sin_table`` are the
     model's fp32 RotaryCache tables [max_positions, D / 2]; ``positions`` int32
     or int64."""
+    if torch.compiler.is_compiling():  # an opaque node for torch.compile
+        res = torch.ops.microinfer_b200.qk_norm_rope_store(
+            qkv, q_weight, k_weight, positions, cos_table, sin_table, key_cache, value_cache,
+            slot_mapping, num_q_heads, num_kv_heads, float(eps), bool(interleaved))
+        return res if out is None else out.copy_(res)
     tokens = qkv.shape[0]
     if key_cache.ndim != 4 or value_cache.shape != key_cache.shape:
         raise ValueError("caches must be matching [blocks, block_size, Hkv, D] tensors")

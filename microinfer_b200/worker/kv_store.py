@@ -40,6 +40,10 @@ def _check_cache(key_cache: torch.Tensor, value_cache: torch.Tensor, keys: torch
 
 def store_kv(key_cache, value_cache, blocks, offsets, keys, values, block_size: int):
     """cache[blocks[t], offsets[t]] = keys[t] (and values); unique slots assumed."""
+    if torch.compiler.is_compiling():  # an opaque node for torch.compile
+        torch.ops.microinfer_b200.store_kv(key_cache, value_cache, blocks, offsets, keys, values,
+                                           block_size)
+        return
     _check_kv_rows(keys, values)
     _check_cache(key_cache, value_cache, keys)
     if block_size != key_cache.shape[1]:
@@ -67,6 +71,9 @@ def store_kv(key_cache, value_cache, blocks, offsets, keys, values, block_size: 
 
 def store_kv_slots(key_cache, value_cache, slots, keys, values):
     """cache[slot // bs, slot % bs] = keys[t] (and values); slot -1 writes nothing."""
+    if torch.compiler.is_compiling():  # an opaque node for torch.compile
+        torch.ops.microinfer_b200.store_kv_slots(key_cache, value_cache, slots, keys, values)
+        return
     _check_kv_rows(keys, values)
     _check_cache(key_cache, value_cache, keys)
     tokens = keys.shape[0]

@@ -353,3 +353,40 @@ def test_bad_records_are_flagged(cuda_device):
     assert status & _lib.DEV_BAD_ROW and status & _lib.DEV_BAD_BLOCK
     assert out_s.tolist() == [-1, -1]
     assert (out_b[0] == -1).all() and int(meta.page_table[0, 0]) == -1
+
+
+@pytest.mark.gpu
+def test_persistent_decode_outputs_feed_a_captured_graph(cuda_device):
+    """As the reference runner does with its decode buffers: capture attention once
+    on the builder's persistent outputs, then each step rebuild the metadata
+    (eager, one launch) and replay; the replay must equal an eager decode."""
+    _lib.read_device_status(cuda_device)
+    bs, nb, hq, hkv, d = 16, 64, 16, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(3)
+    kc = (torch.randn(nb, bs, hkv, d, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    vc = (torch.randn(nb, bs, hkv, d, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    q = torch.randn(3, hq, d, device="cuda", generator=g).to(torch.bfloat16)
+    seqs = []
+    for i, n in enumerate((17, 40, 33)):
+        s = FakeSeq(i)
+        s.token_ids = list(range(n))
+        s.block_table = list(range(i * 8, i * 8 + 4))
+        seqs.append(s)
+    meta = mi.DeviceRunnerMetadata(bs, nb, max_rows=4, max_pages=8, device=cuda_device)
+    _, _, md = meta.prepare_decode(seqs)  # sizes the persistent buffers (width 4)
+    out = torch.empty_like(q)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        mi.paged_decode(q, kc, vc, md.block_tables, md.context_lens, split_k=1, out=out)
+    for step in range(5):
+        for s in seqs:
+            s.token_ids.append(step)
+        _, _, md2 = meta.prepare_decode(seqs)
+        assert md2.block_tables.data_ptr() == md.block_tables.data_ptr()
+        graph.replay()
+        want = mi.paged_decode(q, kc, vc, md2.block_tables.clone(), md2.context_lens.clone(),
+                               split_k=1)
+        torch.cuda.synchronize()
+        assert torch.equal(out, want)
+    assert _lib.read_device_status(cuda_device) == 0
