@@ -5,8 +5,10 @@
 //   q = self.rotary.apply(q, position); same for k   transformer.py:224-225, layer/rope.py:6-21
 //   store_kv(k, v at slot_mapping)                   layer/cached_attention.py:76-85
 // with the reference's rounding points, so the results match its eager ops:
-//   norm: y = round(x * (1 / sqrt(mean(x^2) + eps)) * w), all in fp32, one
-//         rounding to the activation dtype (torch's F.rms_norm);
+//   norm: y = round(x * rsqrt(mean(x^2) + eps) * w), all in fp32, one rounding
+//         to the activation dtype (torch's F.rms_norm; the reciprocal square root
+//         is the hardware one, within 2 ulp of 1/sqrt in fp32 as in torch's CUDA
+//         kernel, so a 16-bit result can rarely differ by one unit from a CPU run);
 //   rope: on the rounded y widened to fp32, split-half
 //           out[i]      = y[i] * cos[j] - y[i + D/2] * sin[j]
 //           out[i+D/2]  = y[i+D/2] * cos[j] + y[i] * sin[j]      (j = i < D/2)
@@ -18,11 +20,12 @@
 // The cos/sin tables are the caller's (the model's RotaryCache, fp32
 // [max_positions, D/2]); nothing here evaluates a trigonometric function.
 //
-// One CTA per token, 8 warps over the token's Hq + 2 Hkv head rows (up to 4
-// rows per warp per pass, all loaded before any is processed, so each warp
-// keeps 4 row loads in flight).  Lane L holds elements [L*E, L*E + E) with
-// E = D/32, so the split-half partner of an element sits in lane L ^ 16 and the
-// interleaved partner in the same lane.  Position, slot, the cos/sin
+// One CTA per token, 2 warps over the token's Hq + 2 Hkv head rows.  A head row
+// spans a group of G = D / E lanes, E = 16 / sizeof(T) elements per lane (one
+// 16-byte vector), so a warp covers 32 / G rows per instruction; each warp
+// loads 8 such row groups before it processes any (4 KB in flight per warp for
+// bf16).  The split-half partner of an element sits in lane ^ G/2 of its group,
+// the interleaved partner in the same lane.  Position, slot, the cos/sin
 // coefficients and the two weight vectors are read once per warp for all of
 // the token's heads.  Products and sums use the packed f32x2 instructions
 // with explicit round-to-nearest (each lane rounded exactly as __fmul_rn /
@@ -38,9 +41,9 @@ namespace mi {
 
 namespace {
 
-constexpr int kPrologueThreads = 256;
+constexpr int kPrologueThreads = 64;
 constexpr int kPrologueWarps = kPrologueThreads / 32;
-constexpr int kRowsPerWarp = 2;  // row groups per warp loaded ahead
+constexpr int kRowsPerWarp = 8;  // row groups per warp loaded ahead
 
 // E consecutive elements of T as one aligned vector.
 template <typename T, int E>
@@ -79,30 +82,20 @@ struct RowVec {
   }
 };
 
-// fp32 -> bf16 round-to-nearest-even with integer operations, the result left
-// in the upper half of an fp32 word (so it is also the widened bf16 value):
-// add 0x7fff plus the lowest kept bit, then clear the low half; a carry into the
-// exponent gives the correctly rounded overflow to infinity.  NaN stays a quiet
-// NaN.  The packed conversion instruction runs on the same pipe as the square
-// root and reciprocal and would bound this kernel; these are plain ALU ops.
-__device__ __forceinline__ uint32_t bf16_rne_bits(float f) {
-  const uint32_t u = __float_as_uint(f);
-  const uint32_t r = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
-  return f != f ? 0x7fc00000u : r;
-}
-
 // Round E fp32 values to T and return them packed; `y` receives the rounded
-// values widened back to fp32.
+// values widened back to fp32 (bf16: one packed conversion per pair, widened
+// back by bit placement).
 template <typename T, int E, typename V>
 __device__ __forceinline__ V round_pack(const float (&x)[E], float (&y)[E]) {
   V v;
-  uint32_t *w = reinterpret_cast<uint32_t *>(&v);
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    uint32_t *w = reinterpret_cast<uint32_t *>(&v);
 #pragma unroll
     for (int i = 0; i < E; i += 2) {
-      const uint32_t lo = bf16_rne_bits(x[i]), hi = bf16_rne_bits(x[i + 1]);
-      y[i] = __uint_as_float(lo), y[i + 1] = __uint_as_float(hi);
-      w[i / 2] = __byte_perm(lo, hi, 0x7632);  // upper halves: element i low, i+1 high
+      const __nv_bfloat162 b = __floats2bfloat162_rn(x[i], x[i + 1]);
+      w[i / 2] = *reinterpret_cast<const uint32_t *>(&b);
+      y[i] = __uint_as_float(w[i / 2] << 16);
+      y[i + 1] = __uint_as_float(w[i / 2] & 0xffff0000u);
     }
   } else {
     T *e = reinterpret_cast<T *>(&v);
@@ -132,7 +125,7 @@ __device__ __forceinline__ void load_f32(const float *src, float (&dst)[N]) {
 }  // namespace
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kPrologueThreads, 3) qk_prologue_kernel(const QkPrologueParams p) {
+__global__ void __launch_bounds__(kPrologueThreads, 10) qk_prologue_kernel(const QkPrologueParams p) {
   constexpr int E = 16 / static_cast<int>(sizeof(T));  // elements per lane: one 16-byte vector
   constexpr int G = D / E;                             // lanes per head row
   constexpr int R = 32 / G;                            // rows one warp instruction covers
@@ -211,7 +204,7 @@ __global__ void __launch_bounds__(kPrologueThreads, 3) qk_prologue_kernel(const 
       for (int i = 0; i < E; ++i) ss = fmaf(x[i], x[i], ss);
 #pragma unroll
       for (int off = G / 2; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      const float inv = 1.f / sqrtf(ss / static_cast<float>(D) + p.eps);
+      const float inv = rsqrtf(ss / static_cast<float>(D) + p.eps);
       float w[E];
       RV::to_float(h < hq ? wq : wk, w);
       // RMSNorm: fp32, one rounding to T (F.rms_norm)
