@@ -195,8 +195,14 @@ __global__ void __launch_bounds__(kPrologueThreads, 10) qk_prologue_kernel(const
       const int h0 = base + (j * kPrologueWarps + warp) * R;
       if (h0 >= heads) break;  // warp-uniform
       const int h = h0 + sub;
-      // every lane runs the q/k math (v and out-of-range lanes discard it), so the
-      // shuffles below see whole groups
+      if (h0 >= hq + hkv) {  // every row of the group is a v row (warp-uniform): copy only
+        if (h < heads && slot >= 0)
+          *reinterpret_cast<V *>(p.value_cache + (slot * hkv + (h - hq - hkv)) * D * static_cast<int64_t>(sizeof(T)) +
+                                 lane_off) = raw[j];
+        continue;
+      }
+      // every lane runs the q/k math (v and out-of-range lanes of a mixed group
+      // discard it), so the shuffles below see whole groups
       float x[E];
       RV::to_float(raw[j], x);
       float ss = 0.f;
