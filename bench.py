@@ -362,7 +362,8 @@ def prefill_kernel_name() -> str:
     one-tile kernel)."""
     if os.environ.get("MICROINFER_B200_PREFILL") == "tc1":
         return "prefill_tc_kernel (tcgen05, one 128-row query tile per CTA)"
-    return "prefill_tc2_kernel (tcgen05, two 128-row query tiles per CTA sharing K/V)"
+    return ("prefill_tc2_kernel (tcgen05, two 128-row query tiles per CTA sharing K/V); "
+            "one-token rows of a mixed batch by paged_decode_mma_kernel launched behind it")
 
 
 def measure_prefill(device, workload: str, layers: int = 28, reps: int = 10):

@@ -701,8 +701,39 @@ static int prefill_common(void *out, const void *query, const void *kbase, const
                   aligned16(kbase) && aligned16(vbase) && aligned16(query) && aligned16(out) &&
                   (paged || (kv_token_stride * e) % 16 == 0);
   if (tc) {
+    // Mixed batch (some sequences have one query token, detectable on the host
+    // when the tokens are fewer than num_seqs * max_seqlen_q, or all of them when
+    // max_seqlen_q == 1): those rows go to the mma decode kernel, launched right
+    // after the prefill kernel as its programmatic dependent, so its CTAs take
+    // the SMs the prefill tail leaves free instead of running M=128 tensor tiles
+    // for one token each.
+    const bool mixed = paged && decode_mma_supported(dtype, head_dim, G, block_size) &&
+                       num_seqs <= 65535 &&
+                       static_cast<uint64_t>(num_blocks) * block_size < (1ull << 31) &&
+                       (max_seqlen_q == 1 || num_tokens < num_seqs * static_cast<int64_t>(max_seqlen_q));
+    p.mixed_decode = mixed ? 1 : 0;
     const cudaError_t te = launch_prefill_tc(p, dtype, G, max_seqlen_q, paged, st);
-    if (te != cudaErrorNotSupported) return cuda_status(te);  // else: shape outside its grid limits
+    if (te == cudaErrorNotSupported) {  // shape outside its grid limits: generic for every row
+      p.mixed_decode = 0;
+      return cuda_status(launch_attn_generic(p, dtype, paged, st));
+    }
+    if (te != cudaSuccess || !mixed) return cuda_status(te);
+    DecodeParams d = {};
+    d.out = out;
+    d.query = query;
+    d.key_cache = static_cast<const char *>(kbase);
+    d.value_cache = static_cast<const char *>(vbase);
+    d.block_tables = block_tables;
+    d.bt_stride = bt_stride;
+    d.num_blocks = num_blocks;
+    d.block_size = block_size;
+    d.num_q_heads = num_q_heads;
+    d.num_kv_heads = num_kv_heads;
+    d.scale_log2 = p.scale_log2;
+    d.status = dev_status;
+    d.cu_q = cu_q;
+    d.cu_k = cu_k;
+    return cuda_status(launch_decode_mma(d, dtype, head_dim, G, num_seqs, 1, st));
   }
   return cuda_status(launch_attn_generic(p, dtype, paged, st));
 }

@@ -170,11 +170,23 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
   }
   __syncwarp();
 
-  // Without early_kv everything below may come from the preceding kernel.
-  if (!p.early_kv) pdl_wait();
+  // Without early_kv everything below may come from the preceding kernel (a
+  // mixed-batch launch needs no wait: see DecodeParams::cu_q).
+  const bool mixed = p.cu_q != nullptr;
+  if (!p.early_kv && !mixed) pdl_wait();
 
   const int split = blockIdx.x, nsplit = gridDim.x;
   const int64_t seq = blockIdx.z;
+  const bool waits_for_prefill = mixed && split == 0 && kvh == 0 && seq == 0;
+  int64_t qo_row = seq;  // query / output row
+  if (mixed) {
+    const int q0 = __ldg(p.cu_q + seq);
+    if (__ldg(p.cu_q + seq + 1) - q0 != 1) {  // uniform: a prefill sequence
+      if (waits_for_prefill) pdl_wait();
+      return;
+    }
+    qo_row = q0;
+  }
   const int32_t *table = p.block_tables + seq * p.bt_stride;
   auto chunk_of = [&](int it) { return split + nsplit * (warp + kWarpsM * it); };
   auto table_entry = [&](int ci) -> int32_t {  // page of chunk ci (block_size % 16 == 0)
@@ -189,7 +201,7 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     const int32_t a = __shfl_sync(kAll, pg_cur, idx & 31), b = __shfl_sync(kAll, pg_nxt, idx & 31);
     return (idx >> 5) == (it_now >> 5) ? a : b;
   };
-  int ctx = __ldg(p.context_lens + seq);
+  int ctx = mixed ? __ldg(p.cu_k + seq + 1) - __ldg(p.cu_k + seq) : __ldg(p.context_lens + seq);
   const int64_t slot = fused ? static_cast<int64_t>(__ldg(p.slot_mapping + seq)) : -1;
   const int64_t cap = p.bt_stride * p.block_size;
   if (ctx > cap) {
@@ -259,7 +271,7 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
   uint32_t qa[C::kKSteps][2];
   {
     const T *qrow = static_cast<const T *>(p.query) +
-                    (seq * p.num_q_heads + static_cast<int64_t>(kvh) * G + (g < G ? g : 0)) * D;
+                    (qo_row * p.num_q_heads + static_cast<int64_t>(kvh) * G + (g < G ? g : 0)) * D;
 #pragma unroll
     for (int ks = 0; ks < C::kKSteps; ++ks) {
       qa[ks][0] = g < G ? *reinterpret_cast<const uint32_t *>(qrow + ks * 16 + 2 * t) : 0u;
@@ -464,13 +476,14 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     }
     const int qh = kvh * G + h;
     if (nsplit == 1) {
-      T *out = static_cast<T *>(p.out) + (seq * p.num_q_heads + qh) * D;
+      T *out = static_cast<T *>(p.out) + (qo_row * p.num_q_heads + qh) * D;
       out[d] = Elem<T>::from_float(L > 0.f ? A / L : 0.f);
     } else {
       split_store_state(p, seq, qh, nsplit, split, D, d, M, L, A);
     }
   }
   if (nsplit > 1) split_arrive_and_merge<T, G, D>(p, seq, kvh, nsplit, last_flag);
+  if (waits_for_prefill) pdl_wait();
 }
 
 namespace {

@@ -66,6 +66,10 @@ struct AttnParams {
   int32_t head_dim;
   float scale_log2;
   int32_t *status;
+  // 1: the tensor-core prefill kernel leaves sequences with one query token to
+  // the decode kernel launched after it (mixed batches), and lets that launch
+  // start as soon as all its CTAs are running.
+  int32_t mixed_decode;
 };
 struct DecodeParams {
   void *out;
@@ -96,6 +100,16 @@ struct DecodeParams {
   // token are treated as produced by the preceding kernel; the caller
   // guarantees that kernel does not write the pool, tables or lengths.
   int32_t early_kv;
+  // Decode rows of a mixed prefill batch (cu_q != nullptr): sequence s is handled
+  // only if cu_q[s+1] - cu_q[s] == 1 (the prefill kernel skips exactly those); its
+  // query and output row is token cu_q[s] and its context cu_k[s+1] - cu_k[s]
+  // (context_lens unused).  This launch follows the prefill kernel as its
+  // programmatic dependent and starts once every prefill CTA has passed its own
+  // dependency wait, so everything it reads is complete: it does not wait before
+  // working.  Block (0, 0, 0) waits for the prefill grid before exiting, so this
+  // grid completes only after the prefill grid (the next kernel's wait covers both).
+  const int32_t *cu_q;
+  const int32_t *cu_k;
 };
 
 // Attention prologue (qk_prologue.cu): q/k RMSNorm + RoPE, k/v store.

@@ -66,6 +66,10 @@ struct __align__(64) PrefillTcParams {
   int32_t paged;
   float scale_log2;
   int32_t *status;
+  // Mixed batches: sequences with one query token are left to the decode kernel
+  // launched right after this one, which may start once every CTA here has passed
+  // its dependency wait (so the trigger comes early).
+  int32_t skip_single;
 };
 
 namespace {
@@ -154,10 +158,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_co
   const int64_t seq = blockIdx.z;
 
   pdl_wait();
+  if (p.skip_single) pdl_launch_dependents();
   const int q_start = p.cu_q[seq];
   const int q_len = p.cu_q[seq + 1] - q_start;
   const int t0 = qt * TQ;
   if (t0 >= q_len) return;  // uniform: this sequence has fewer query tiles
+  if (p.skip_single && q_len == 1) return;  // a decode row: the decode launch handles it
   const int kv0 = p.cu_k[seq];
   const int ctx = p.cu_k[seq + 1] - kv0;
   const int prefix = ctx - q_len;
@@ -565,10 +571,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
   const int64_t seq = blockIdx.z;
 
   pdl_wait();
+  if (p.skip_single) pdl_launch_dependents();
   const int q_start = p.cu_q[seq];
   const int q_len = p.cu_q[seq + 1] - q_start;
   const int t0 = blockIdx.x * 2 * TQ;
   if (t0 >= q_len) return;  // uniform: this sequence has fewer tile pairs
+  if (p.skip_single && q_len == 1) return;  // a decode row: the decode launch handles it
   const int kv0 = p.cu_k[seq];
   const int ctx = p.cu_k[seq + 1] - kv0;
   const int prefix = ctx - q_len;
@@ -983,6 +991,7 @@ cudaError_t launch_prefill_tc(const AttnParams &a, int dtype, int G, int32_t max
   p.paged = paged ? 1 : 0;
   p.scale_log2 = a.scale_log2;
   p.status = a.status;
+  p.skip_single = paged && a.mixed_decode ? 1 : 0;
   const int64_t n = a.num_seqs;
   if (dtype == MI_DTYPE_BFLOAT16) {
     switch (G) {
