@@ -523,7 +523,8 @@ def measure_prologue(device, tokens: int = 8192, layers: int = 8, reps: int = 20
     del pool, qkv, q_out
     return {"workload": f"Qwen3-0.6B attention prologue, {tokens} tokens (BASELINE configs[3] "
                         "prefill batch), bf16, split-half RoPE",
-            "kernel": "qk_prologue_kernel (RMSNorm q/k + RoPE + k/v store, one launch)",
+            "kernel": "qk_prologue_stream_kernel (RMSNorm q/k + RoPE + k/v store, one launch; "
+                      "rows staged through shared memory by bulk copies)",
             "us_per_layer": round(ms_fused * 1e3, 2), "bytes_per_launch": nbytes,
             "gbs": round(gbs, 1), "hbm_frac": round(gbs / peaks["hbm_gbs"], 4),
             "peak_source": f"hbm_gbs of {src}",

@@ -186,7 +186,10 @@ def _torch_prologue(qkv, q_weight, k_weight, positions, cos, sin, hq, hkv, d, ep
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", ["bf16", "f16", "f32"])
 @pytest.mark.parametrize("d,hq,hkv,interleaved", [(128, 16, 8, False), (128, 32, 8, True),
-                                                  (64, 8, 1, False), (64, 16, 4, True)])
+                                                  (64, 8, 1, False), (64, 16, 4, True),
+                                                  # rows too wide for the shared-memory stages
+                                                  # in fp32: the register form
+                                                  (128, 96, 16, False), (128, 96, 16, True)])
 @pytest.mark.parametrize("tokens", [1, 37, 1500])
 def test_kernel_matches_torch_ops(dtype, d, hq, hkv, interleaved, tokens, clean_status):
     tdt = _torch_dtype(dtype)
