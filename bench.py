@@ -1099,6 +1099,33 @@ def run_profile(args):
         print(json.dumps({"profile": "long", "kernel": kernel, "split_k": split,
                           "decode_bytes_per_launch": decode_bytes([ctx_len], hq, hkv, D, 2, BS)}))
         return
+    if args.profile == "metadata":
+        # decode metadata for 256 sequences (contexts U[128, 512]) over `--steps` steps
+        import numpy as np
+
+        class _Seq:
+            def __init__(self, sid, n, table):
+                self.seq_id, self.num_tokens, self.block_table = sid, n, table
+                self.last_token, self.num_cached_tokens, self.num_scheduled_tokens = 1, n - 1, 1
+
+        rng = np.random.default_rng(256)
+        nb = 256 * 40
+        perm = rng.permutation(nb).tolist()
+        seqs = []
+        for i in range(256):
+            n = int(rng.integers(128, 512))
+            seqs.append(_Seq(i, n, [perm.pop() for _ in range((n + BS - 1) // BS + 1)]))
+        meta = mi.DeviceRunnerMetadata(BS, nb, max_rows=256, max_pages=40, device=device)
+        for _ in range(args.steps):
+            meta.prepare_decode(seqs)
+            for s_ in seqs:
+                s_.num_tokens += 1
+                if (s_.num_tokens - 1) // BS >= len(s_.block_table):
+                    s_.block_table.append(perm.pop())
+        torch.cuda.synchronize(device)
+        mi.check_device_status(device)
+        print(json.dumps({"profile": "metadata", "sequences": 256, "steps": args.steps}))
+        return
     if args.profile == "prologue":
         g = torch.Generator(device=device).manual_seed(21)
         layers, tokens = 2, 8192
@@ -1169,7 +1196,7 @@ def main():
                     help="reference = the reference's CPU path (oracle port); reference-gpu = "
                          "its Triton kernels on this GPU (needs baseline/_ref)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["decode", "long", "prefill", "mixed", "prologue"], default=None,
+    ap.add_argument("--profile", choices=["decode", "long", "prefill", "mixed", "prologue", "metadata"], default=None,
                     help="run a small eager case for ncu instead of the benchmark")
     ap.add_argument("--split-k", type=int, default=0)
     args = ap.parse_args()

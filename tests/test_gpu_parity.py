@@ -113,6 +113,35 @@ def test_attention_matches_reference_and_oracle(name):
     assert_close(out, expected, dt)
 
 
+MIXED = ["mixed_bf16"] + [c for c in cases.CASES if c.startswith("tc_prefill_g")]
+
+
+@pytest.mark.parametrize("name", MIXED)
+def test_mixed_batch_decode_rows_through_the_c_abi(name):
+    """Mixed batches: the one-token rows run on the decode kernel launched behind
+    the tensor-core prefill (its programmatic dependent); called twice in a row
+    through mi_paged_prefill, every row matches the reference."""
+    case = cases.build(name)
+    gold = load_golden(name)
+    dt = case["dtype"]
+    layer = _store(case)
+    q = dev(case["query"], dt)
+    table = dev(case["block_tables"])
+    cu_q, cu_k = dev(case["cu_seqlens_q"]), dev(case["cu_seqlens_k"])
+    n = len(case["contexts"])
+    hq, d = q.shape[1], q.shape[2]
+    nb, bs, hkv, _ = layer.keys.shape
+    for _ in range(2):
+        out = torch.full_like(q, float("nan"))
+        _lib.call("mi_paged_prefill", out.data_ptr(), q.data_ptr(), layer.keys.data_ptr(),
+                  layer.values.data_ptr(), nb, bs, hq, hkv, d, _lib.dtype_code(q.dtype),
+                  cu_q.data_ptr(), cu_k.data_ptr(), table.data_ptr(), table.stride(0), n,
+                  q.shape[0], int(case["q_lens"].max()), float(case["scale"]),
+                  _lib.status_buffer(q.device).data_ptr(), _lib.stream_of(q.device))
+        torch.cuda.synchronize()
+        assert_close(out, gold["out"], dt)
+
+
 @pytest.mark.parametrize("name", [c for c in PAGED if cases.kind(c) == "decode"])
 @pytest.mark.parametrize("split_k", [1, 2, 3, 7, 37])
 def test_decode_split_k_matches_reference(name, split_k):
