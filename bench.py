@@ -594,9 +594,52 @@ def measure_runner_metadata(device, reps: int = 200):
         res[label] = {"device_builder_us": round(ours_us, 1),
                       "host_assembly_us": round(base_us, 1),
                       "speedup": round(base_us / ours_us, 2)}
-    return {"what": "decode metadata ready on the device, per step (median wall time incl. "
+
+    # prefill metadata, BASELINE configs[3] shapes: 64 sequences, 128-token suffixes
+    # on a cached 1024-token prefix (8192 tokens, block tables needed)
+    from oracle.runner_oracle import staged_prefill
+
+    class _PSeq:
+        def __init__(self, sid, tokens, table):
+            self.seq_id, self.token_ids, self.block_table = sid, tokens, table
+            self.num_tokens = len(tokens)
+            self.num_cached_tokens, self.num_scheduled_tokens = 1024, 128
+
+        def __getitem__(self, key):
+            return self.token_ids[key]
+
+        def __len__(self):
+            return self.num_tokens
+
+    rng = np.random.default_rng(64)
+    prefix_pages = list(range(64))
+    pseqs = [_PSeq(i, [int(x) for x in rng.integers(0, 150000, 1152)],
+                   prefix_pages + list(range(64 + 8 * i, 72 + 8 * i))) for i in range(64)]
+    nb = 64 + 8 * 64
+    times_o, times_b = [], []
+    builder = mi.DeviceRunnerMetadata(BS, nb, max_rows=64, max_pages=72, device=device)
+    for k in range(23):
+        for sq in pseqs:  # new sequences each step: every table is sent whole
+            builder.release(sq)
+        t0 = time.perf_counter()
+        builder.prepare_prefill(pseqs)
+        torch.cuda.synchronize(device)
+        t1 = time.perf_counter()
+        staged_prefill(pseqs, BS, device)
+        torch.cuda.synchronize(device)
+        t2 = time.perf_counter()
+        if k >= 3:
+            times_o.append(t1 - t0)
+            times_b.append(t2 - t1)
+    mi.check_device_status(device)
+    ours_us, base_us = statistics.median(times_o) * 1e6, statistics.median(times_b) * 1e6
+    res["prefill_b64_q128_prefix1024"] = {"device_builder_us": round(ours_us, 1),
+                                          "host_assembly_us": round(base_us, 1),
+                                          "speedup": round(base_us / ours_us, 2)}
+    return {"what": "metadata ready on the device, per step (median wall time incl. "
                     "synchronize); device builder vs the reference runner's host assembly "
-                    "restated", "rows": res}
+                    "restated (decode rows: _fill_decode_rows + copies; prefill row: "
+                    "prepare_prefill)", "rows": res}
 
 
 def run_reference(args):

@@ -45,6 +45,40 @@ from microinfer_b200.layer.metadata import AttentionMetadata
 RECORD = 6  # int32 per sequence: row, a, b, num_pages, update_begin, update_count
 
 
+class _Updates:
+    """Page-table changes of one step as (column, page) int32 pairs, kept as two
+    flat lists so whole tables (sequences new to their row) join with C-level
+    list operations and become one array at the end.  Single entries are range
+    checked as they are added, whole tables once in ``array``."""
+
+    __slots__ = ("cols", "pages", "unchecked")
+
+    def __init__(self):
+        self.cols: list = []
+        self.pages: list = []
+        self.unchecked = False
+
+    def __len__(self) -> int:
+        return len(self.cols)
+
+    def add(self, col: int, page: int):
+        self.cols.append(col)
+        self.pages.append(page)
+
+    def add_table(self, table):
+        self.cols.extend(range(len(table)))
+        self.pages.extend(table)
+        self.unchecked = True
+
+    def array(self, num_blocks: int) -> np.ndarray:
+        if not self.cols:
+            return np.empty((0, 2), dtype=np.int32)
+        a = np.array((self.cols, self.pages), dtype=np.int64)
+        if self.unchecked and (a[1].min() < 0 or a[1].max() >= num_blocks):
+            raise ValueError("block id outside the pool")
+        return np.ascontiguousarray(a.T, dtype=np.int32)
+
+
 def _seq_key(seq):
     key = getattr(seq, "seq_id", None)
     return id(seq) if key is None else key
@@ -110,7 +144,7 @@ class DeviceRunnerMetadata:
     def num_free_rows(self) -> int:
         return len(self._free_rows)
 
-    def _changes(self, seq, row: int, first_pos: int, updates: list, commits: list) -> int:
+    def _changes(self, seq, row: int, first_pos: int, updates: _Updates, commits: list) -> int:
         """Append (column, page) pairs for the entries of ``seq``'s table that the
         device does not hold yet; returns the number appended.  What the device
         will hold after the launch is queued in ``commits`` and recorded only once
@@ -126,15 +160,18 @@ class DeviceRunnerMetadata:
                 raise ValueError("a page before the first scheduled token changed")
         else:
             k0 = min(len(sent), max(first_pos, 0) // self.block_size)
-        n0 = len(updates)
-        for col in range(k0, len(table)):
-            page = table[col]
-            if col >= len(sent) or sent[col] != page:
-                if not 0 <= page < self.num_blocks:
-                    raise ValueError(f"block id {page} outside the pool")
-                updates.append((col, page))
+        n0 = len(updates.cols)
+        if not sent:  # a row new to this sequence: the whole table (checked in array())
+            updates.add_table(table)
+        else:
+            for col in range(k0, len(table)):
+                page = table[col]
+                if col >= len(sent) or sent[col] != page:
+                    if not 0 <= page < self.num_blocks:
+                        raise ValueError(f"block id {page} outside the pool")
+                    updates.add(col, page)
         commits.append((row, k0, list(table[k0:])))
-        return len(updates) - n0
+        return len(updates.cols) - n0
 
     def _commit(self, commits: list):
         for row, k0, tail in commits:
@@ -208,7 +245,7 @@ class DeviceRunnerMetadata:
             raise ValueError("a scheduled batch must contain requests")
         bs, rows, sent_all, verify = self.block_size, self._rows, self._sent, self.verify
         flat: list = []
-        updates: list = []
+        updates = _Updates()
         commits: list = []
         seen: set = set()
         width = 0
@@ -226,10 +263,10 @@ class DeviceRunnerMetadata:
                 raise ValueError("a sequence appears twice in the batch")
             seen.add(row)
             sent = sent_all[row]
-            begin = len(updates)
+            begin = len(updates.cols)
             if verify or sent[k:] != table[k:]:  # usually one entry compared
                 self._changes(seq, row, n - 1, updates, commits)
-            flat += (row, n, seq.last_token, pages, begin, len(updates) - begin)
+            flat += (row, n, seq.last_token, pages, begin, len(updates.cols) - begin)
             if pages > width:
                 width = pages
         try:
@@ -238,8 +275,7 @@ class DeviceRunnerMetadata:
             raise ValueError("token ids must be nonnegative int32 values") from None
         if rec[:, 2].min() < 0:
             raise ValueError("token ids must be nonnegative int32 values")
-        return {"records": rec, "updates": np.asarray(updates, dtype=np.int32).reshape(-1, 2),
-                "width": width, "commits": commits}
+        return {"records": rec, "updates": updates.array(self.num_blocks), "width": width, "commits": commits}
 
     def prepare_decode(self, seqs):
         """``ModelRunner.prepare_decode``: last token, position ``len - 1``, its
@@ -265,7 +301,7 @@ class DeviceRunnerMetadata:
         if batch == 0:
             raise ValueError("a scheduled batch must contain requests")
         rec = np.empty((batch, RECORD), dtype=np.int32)
-        updates: list = []
+        updates = _Updates()
         commits: list = []
         tokens = []
         seen = set()
@@ -283,20 +319,20 @@ class DeviceRunnerMetadata:
             if row in seen:
                 raise ValueError("a sequence appears twice in the batch")
             seen.add(row)
-            begin = len(updates)
+            begin = len(updates.cols)
             count = self._changes(seq, row, start, updates, commits)
             rec[i] = (row, start, end, pages, begin, count)
-            tokens.append(np.asarray(seq[start:end], dtype=np.int64))
+            tokens.extend(seq[start:end])
             width = max(width, pages)
             max_q = max(max_q, end - start)
             max_k = max(max_k, end)
             any_cached = any_cached or start > 0
-        ids = np.concatenate(tokens)
+        ids = np.array(tokens, dtype=np.int64)
         if ids.size and (ids.min() < 0 or ids.max() > 2**31 - 1):
             raise ValueError("token ids must be nonnegative int32 values")
         if ids.size > 2**31 - 1:
             raise ValueError("too many scheduled tokens")
-        return {"records": rec, "updates": np.asarray(updates, dtype=np.int32).reshape(-1, 2),
+        return {"records": rec, "updates": updates.array(self.num_blocks),
                 "tokens": ids.astype(np.int32), "table_width": width if any_cached else 0,
                 "max_q": max_q, "max_k": max_k, "commits": commits}
 

@@ -119,3 +119,37 @@ class StagedDecodeRows:
         for k in ("input_ids", "positions", "slot_mapping", "context_lens", "block_tables"):
             self.dev[k][:batch].copy_(h[k][:batch], non_blocking=self.pin)
         return self.dev["input_ids"][:batch], self.dev["positions"][:batch]
+
+
+def staged_prefill(seqs, block_size: int, device):
+    """Timing baseline only: the reference runner's ``prepare_prefill``
+    (runner.py:298-346) restated -- Python lists of every scheduled token's id,
+    position and slot, cumulative lengths, the -1 padded block tables when some
+    sequence has cached tokens, each built into a device tensor.  ``seqs`` are
+    objects with ``token_ids``, ``block_table``, ``num_cached_tokens`` and
+    ``num_scheduled_tokens``.  ``bench.py`` times it beside the device builder."""
+    import torch
+
+    ids, positions, slots, cu_q, cu_k = [], [], [], [0], [0]
+    for seq in seqs:
+        start = seq.num_cached_tokens
+        end = start + seq.num_scheduled_tokens
+        ids.extend(seq.token_ids[start:end])
+        positions.extend(range(start, end))
+        cu_q.append(cu_q[-1] + end - start)
+        cu_k.append(cu_k[-1] + end)
+        table = seq.block_table
+        slots.extend(table[p // block_size] * block_size + p % block_size for p in range(start, end))
+    out = {
+        "cu_q": torch.tensor(cu_q, dtype=torch.int32, device=device),
+        "cu_k": torch.tensor(cu_k, dtype=torch.int32, device=device),
+        "slot_mapping": torch.tensor(slots, dtype=torch.int32, device=device),
+        "input_ids": torch.tensor(ids, dtype=torch.int64, device=device),
+        "positions": torch.tensor(positions, dtype=torch.int64, device=device),
+    }
+    if any(s.num_cached_tokens for s in seqs):
+        width = max(len(s.block_table) for s in seqs)
+        out["block_tables"] = torch.tensor(
+            [list(s.block_table) + [-1] * (width - len(s.block_table)) for s in seqs],
+            dtype=torch.int32, device=device)
+    return out
