@@ -70,6 +70,13 @@ struct __align__(64) PrefillTcParams {
   // launched right after this one, which may start once every CTA here has passed
   // its dependency wait (so the trigger comes early).
   int32_t skip_single;
+  // prefill_tc2_kernel's 1-D grid: work units (seq, kv head, tile pair) in the
+  // order tile pair, kv head, sequence; units from split_from on run as two
+  // single-tile CTAs each, so a last wave that would be less than half full
+  // of pairs becomes one wave of single tiles.
+  int32_t pairs_per_seq;
+  int32_t num_kv_heads;
+  int64_t split_from;
 };
 
 namespace {
@@ -567,20 +574,25 @@ __global__ void __launch_bounds__(kThreads2, 1)
   const uint32_t sV = smem_addr(smem + kOffV2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kvh = blockIdx.y;
-  const int64_t seq = blockIdx.z;
+  const int64_t cta = blockIdx.x;
+  const bool single = cta >= p.split_from;
+  const int64_t unit = single ? p.split_from + (cta - p.split_from) / 2 : cta;
+  const int half = single ? static_cast<int>((cta - p.split_from) & 1) : 0;
+  const int pair = static_cast<int>(unit % p.pairs_per_seq);
+  const int kvh = static_cast<int>((unit / p.pairs_per_seq) % p.num_kv_heads);
+  const int64_t seq = unit / (static_cast<int64_t>(p.pairs_per_seq) * p.num_kv_heads);
 
   pdl_wait();
   if (p.skip_single) pdl_launch_dependents();
   const int q_start = p.cu_q[seq];
   const int q_len = p.cu_q[seq + 1] - q_start;
-  const int t0 = blockIdx.x * 2 * TQ;
+  const int t0 = pair * 2 * TQ + half * TQ;
   if (t0 >= q_len) return;  // uniform: this sequence has fewer tile pairs
   if (p.skip_single && q_len == 1) return;  // a decode row: the decode launch handles it
   const int kv0 = p.cu_k[seq];
   const int ctx = p.cu_k[seq + 1] - kv0;
   const int prefix = ctx - q_len;
-  const int nt[2] = {min(TQ, q_len - t0), max(0, min(TQ, q_len - t0 - TQ))};
+  const int nt[2] = {min(TQ, q_len - t0), single ? 0 : max(0, min(TQ, q_len - t0 - TQ))};
   int nkv_t[2];
 #pragma unroll
   for (int x = 0; x < 2; ++x) {
@@ -923,8 +935,16 @@ cudaError_t launch_tg2(PrefillTcParams &p, int num_kv_heads, int64_t num_seqs, i
     attr_set[dev] = true;
   }
   constexpr int TQ = 128 / G;
-  const dim3 grid((max_seqlen_q + 2 * TQ - 1) / (2 * TQ), num_kv_heads, static_cast<unsigned>(num_seqs));
-  return launch_pdl(kern, grid, dim3(kThreads2), kSmemBytes2, stream, p);
+  const int64_t pairs = (max_seqlen_q + 2 * TQ - 1) / (2 * TQ);
+  const int64_t units = pairs * num_kv_heads * num_seqs;
+  const int64_t sms = sm_count_current();
+  const int64_t rem = units % sms;  // pair units of the last (partial) wave
+  const int64_t split = units > sms && rem > 0 && 2 * rem <= sms ? rem : 0;
+  if (units + split > 0x7fffffff) return cudaErrorNotSupported;
+  p.pairs_per_seq = static_cast<int32_t>(pairs);
+  p.num_kv_heads = num_kv_heads;
+  p.split_from = units - split;
+  return launch_pdl(kern, dim3(static_cast<unsigned>(units + split)), dim3(kThreads2), kSmemBytes2, stream, p);
 }
 
 // Two query tiles per CTA unless MICROINFER_B200_PREFILL=tc1 pins the
