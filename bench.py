@@ -47,7 +47,7 @@ WORKLOAD = "BASELINE configs[1]: Qwen3-0.6B decode step, bf16, 28 layers, batch 
 
 # kernel names for the roofline entry and the ncu summaries that measured them
 DECODE_KERNEL_NAMES = {"mma": "paged_decode_mma_kernel", "simt": "paged_decode_kernel",
-                       "tcgen05": "paged_decode_tc_kernel", "generic": "attn_generic_kernel"}
+                       "generic": "attn_generic_kernel"}
 DECODE_PROFILES = {"mma": "decode_mma_qwen3_0.6b_config2.md"}
 
 
@@ -365,10 +365,7 @@ def _prefill_batch(workload: str, device, g):
 
 
 def prefill_kernel_name() -> str:
-    """The tcgen05 prefill kernel the library launches (MICROINFER_B200_PREFILL=tc1 pins the
-    one-tile kernel)."""
-    if os.environ.get("MICROINFER_B200_PREFILL") == "tc1":
-        return "prefill_tc_kernel (tcgen05, one 128-row query tile per CTA)"
+    """The tcgen05 prefill kernel the library launches."""
     return ("prefill_tc2_kernel (tcgen05, two 128-row query tiles per CTA sharing K/V); "
             "one-token rows of a mixed batch by paged_decode_mma_kernel launched behind it")
 

@@ -230,11 +230,11 @@ MI_API int mi_paged_decode_uses_workspace(int32_t num_splits);
 /*
  * Launch plan of mi_paged_decode / mi_paged_decode_store for a shape with
  * 16-byte aligned tensors: returns the kernel (1 generic, 2 SIMT bulk-copy,
- * 3 tcgen05 swap-AB, 4 warp-level mma tensor-core) and writes the split
+ * 4 warp-level mma tensor-core) and writes the split
  * count it will use for `num_splits` (0 = automatic) and the workspace bytes
  * the caller must pass.  The mma kernel runs bf16/fp16 with head_dim 64 or
  * 128, a GQA group of 1, 2, 4 or 8 and block_size a multiple of 16; other
- * fast shapes run the SIMT kernel; MICROINFER_B200_DECODE=simt|tc|mma pins
+ * fast shapes run the SIMT kernel; MICROINFER_B200_DECODE=simt|mma pins
  * one.  Automatic splits are mi_paged_decode_default_splits, except that the
  * mma kernel (one CTA per SM) takes one split once num_seqs * num_kv_heads
  * exceeds half the SMs.
@@ -288,9 +288,12 @@ MI_API int mi_paged_decode_store(void *out, const void *query, void *key_cache,
  * that owns only the buffers it was given).  Same arguments and results as
  * mi_paged_decode without the workspace: split-K states go to a 2 MiB scratch
  * array built into the library (held by every GPU that loads it until exit).
- * Limit: num_seqs * num_q_heads * num_splits * (head_dim + 2) * 4 bytes must
- * fit in 2 MiB, else MI_ERR_INVALID.  The first call on a device looks up the
- * array's device address (make it outside stream capture).  Calls share the
+ * Limit: 64 KiB + num_seqs * num_q_heads * num_splits * (head_dim + 2) * 4
+ * bytes must fit in 2 MiB; an explicit num_splits that does not fit gives
+ * MI_ERR_INVALID, num_splits = 0 takes the default split count capped to what
+ * fits (one split needs no scratch).  The first call on a device looks up the
+ * array's device address (make it outside stream capture; a failed lookup is
+ * retried on the next call).  Calls share the
  * array, so calls that overlap on the GPU race; serialise them.  Calls no
  * cudaMalloc/cudaFree.
  */

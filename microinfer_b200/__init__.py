@@ -20,7 +20,7 @@ reference's attention-backend interface:
 """
 
 from microinfer_b200._lib import check_device_status, load, read_device_status
-from microinfer_b200.install import install
+from microinfer_b200.install import install, uninstall
 from microinfer_b200.layer.metadata import AttentionMetadata
 from microinfer_b200.layer.paged_attention import (
     decode_plan,
@@ -50,6 +50,7 @@ __all__ = [
     "decode_plan",
     "gather_paged_kv",
     "install",
+    "uninstall",
     "load",
     "paged_attention_meta",
     "paged_decode",

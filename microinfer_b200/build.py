@@ -20,7 +20,7 @@ LIB_NAME = "libmicroinfer_b200.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 BUILD_DIR = PKG_DIR.parent / "_build"
 
-SOURCES = ["capi.cu", "copy_kernels.cu", "attention.cu", "decode.cu", "decode_tc.cu",
+SOURCES = ["capi.cu", "copy_kernels.cu", "attention.cu", "decode.cu",
            "decode_mma.cu", "prefill_tc.cu", "decode_noalloc.cu", "qk_prologue.cu", "runner_meta.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [

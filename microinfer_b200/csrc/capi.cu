@@ -22,15 +22,12 @@ cudaError_t launch_wait_flag(const int32_t *flag, int64_t timeout_ns, int32_t *s
                              cudaStream_t stream);
 cudaError_t launch_attn_generic(const AttnParams &p, int dtype, bool paged, cudaStream_t stream);
 bool decode_fast_supported(int dtype, int D, int G);
-bool decode_tc_supported(int dtype, int D, int G, int block_size);
 bool decode_mma_supported(int dtype, int D, int G, int block_size);
 cudaError_t launch_qk_prologue(const QkPrologueParams &p, int dtype, int D, cudaStream_t stream);
 cudaError_t launch_decode_meta(const RunnerMetaParams &p, cudaStream_t stream);
 cudaError_t launch_prefill_meta(const RunnerMetaParams &p, cudaStream_t stream);
 cudaError_t launch_decode_mma(const DecodeParams &d, int dtype, int D, int G, int64_t num_seqs,
                               int nsplit, cudaStream_t stream);
-cudaError_t launch_decode_tc(const DecodeParams &d, int dtype, int G, int64_t num_seqs,
-                             int64_t num_blocks, int nsplit, cudaStream_t stream);
 cudaError_t launch_decode_fast(const DecodeParams &p, int dtype, int D, int G, int64_t num_seqs,
                                int nsplit, bool wide, cudaStream_t stream);
 bool decode_wide_supported(int dtype, int D, int G);
@@ -412,29 +409,26 @@ bool decode_uses_workspace(int nsplit) { return nsplit > 1; }
 
 // Decode kernels, in order of preference: warp-level tensor-core MMA
 // (mma.sync, bf16/fp16, D 64/128, block size a multiple of 16), SIMT
-// (TMA-staged, CUDA cores, every fast shape), generic (any shape).  The
-// tcgen05 swap-AB kernel (D=128) is kept behind MICROINFER_B200_DECODE=tc;
-// =simt and =mma pin those kernels.
-constexpr int kDecodeGeneric = 1, kDecodeSimt = 2, kDecodeTc = 3, kDecodeMma = 4;
+// (TMA-staged, CUDA cores, every fast shape), generic (any shape).
+// MICROINFER_B200_DECODE=simt|mma pins one of the fast kernels.
+constexpr int kDecodeGeneric = 1, kDecodeSimt = 2, kDecodeMma = 4;
 
 int decode_kernel_for(int dtype, int D, int G, int block_size, bool aligned, int64_t max_context) {
   (void)max_context;
   static const int mode = [] {
     const char *v = std::getenv("MICROINFER_B200_DECODE");
     if (v != nullptr && std::strcmp(v, "simt") == 0) return 1;
-    if (v != nullptr && std::strcmp(v, "tc") == 0) return 2;
     if (v != nullptr && std::strcmp(v, "mma") == 0) return 3;
     return 0;
   }();
   if (!aligned || !decode_fast_supported(dtype, D, G)) return kDecodeGeneric;
-  if (mode == 2 && decode_tc_supported(dtype, D, G, block_size)) return kDecodeTc;
   if (mode == 1) return kDecodeSimt;
   if (decode_mma_supported(dtype, D, G, block_size)) return kDecodeMma;
   return kDecodeSimt;
 }
 
-// Split count: the caller's, else enough CTAs for one wave (the tcgen05
-// kernel holds one CTA per SM, the SIMT kernel two).
+// Split count: the caller's, else enough CTAs for one wave (the mma kernel
+// holds one CTA per SM, the SIMT kernel two).
 int decode_splits_for(int kernel, int64_t num_seqs, int num_kv_heads, int num_splits, int dev,
                       int64_t ctx_bound) {
   if (num_splits > 0) return num_splits;
@@ -446,15 +440,8 @@ int decode_splits_for(int kernel, int64_t num_seqs, int num_kv_heads, int num_sp
     // 6.2-45 us per layer for contexts 512-4096, 2 splits 13-52 us).
     return 1;
   }
-  if (kernel == kDecodeSimt || kernel == kDecodeMma) {
-    const int64_t hint = ctx_bound > INT32_MAX ? INT32_MAX : ctx_bound;
-    return mi_paged_decode_default_splits(num_seqs, num_kv_heads, static_cast<int32_t>(hint), dev);
-  }
-  const int64_t base = num_seqs * num_kv_heads;
-  int64_t s = sm_count_of(dev) / base;
-  if (s < 1) s = 1;
-  if (s > 64) s = 64;
-  return static_cast<int>(s);
+  const int64_t hint = ctx_bound > INT32_MAX ? INT32_MAX : ctx_bound;
+  return mi_paged_decode_default_splits(num_seqs, num_kv_heads, static_cast<int32_t>(hint), dev);
 }
 
 struct NewToken {
@@ -580,10 +567,6 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
   }
   if (flags & MI_DECODE_EARLY_KV) {
     p.early_kv = 1;
-  }
-  if (kernel == kDecodeTc) {
-    const cudaError_t te = launch_decode_tc(p, dtype, G, num_seqs, num_blocks, nsplit, st);
-    if (te != cudaErrorNotSupported) return cuda_status(te);
   }
   if (kernel == kDecodeMma) {
     const cudaError_t me = launch_decode_mma(p, dtype, head_dim, G, num_seqs, nsplit, st);

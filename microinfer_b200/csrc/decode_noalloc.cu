@@ -12,14 +12,17 @@
 // The scratch is a file-scope __device__ array of kNoAllocScratchBytes (2 MiB)
 // that every GPU loading the library holds until the process exits.  Host
 // code cannot use the array's name as a device address, so on the first call
-// on each device (with that device current) its address is looked up once
-// with cudaGetSymbolAddress and cached; make that first call outside any
-// stream capture.  All calls share the one array.  It starts zeroed (static
-// storage), the split-K arrival counters at its start are left at zero by
-// every launch, and every split state is written before it is read, so
-// nothing needs clearing between calls; calls that overlap on the GPU (two
-// streams, or two threads) race on the array and must be serialised by the
-// caller.
+// on each device (with that device current) its address is looked up with
+// cudaGetSymbolAddress and cached; make that first call outside any stream
+// capture.  A failed lookup is not cached: the next call tries again.  With
+// num_splits = 0 the split count is the library default capped to what the
+// scratch holds (down to one split, which needs no scratch); an explicit
+// split count that does not fit is rejected.  All calls share the one array.
+// It starts zeroed (static storage), the split-K arrival counters at its start
+// are left at zero by every launch, and every split state is written before it
+// is read, so nothing needs clearing between calls; calls that overlap on the
+// GPU (two streams, or two threads) race on the array and must be serialised
+// by the caller.
 #include <mutex>
 
 #include "common.cuh"
@@ -45,24 +48,27 @@ namespace {
 
 constexpr int kMaxDevices = 64;
 float *g_scratch_ptr[kMaxDevices];
-cudaError_t g_scratch_err[kMaxDevices];
-std::once_flag g_scratch_once[kMaxDevices];
+std::mutex g_scratch_mutex;
 
-// Device address of the scratch array on the current device (looked up once).
+// Device address of the scratch array on the current device.  Only a
+// successful lookup is kept; a failed one (for instance made while a stream
+// capture was active) clears its non-sticky error and is retried next call.
 int scratch_address(float **out) {
   int dev = 0;
   const cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return capi_fail(static_cast<int>(e), "cudaGetDevice failed");
   if (dev < 0 || dev >= kMaxDevices) return capi_fail(MI_ERR_UNSUPPORTED, "device index >= 64");
-  std::call_once(g_scratch_once[dev], [dev] {
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
     void *ptr = nullptr;
-    g_scratch_err[dev] = cudaGetSymbolAddress(&ptr, g_decode_scratch);
+    const cudaError_t se = cudaGetSymbolAddress(&ptr, g_decode_scratch);
+    if (se != cudaSuccess || ptr == nullptr) {
+      cudaGetLastError();
+      return capi_fail(static_cast<int>(se != cudaSuccess ? se : cudaErrorInvalidSymbol),
+                       "cudaGetSymbolAddress of the decode scratch array failed");
+    }
     g_scratch_ptr[dev] = static_cast<float *>(ptr);
-  });
-  if (g_scratch_err[dev] != cudaSuccess || g_scratch_ptr[dev] == nullptr)
-    return capi_fail(static_cast<int>(g_scratch_err[dev] != cudaSuccess ? g_scratch_err[dev]
-                                                                        : cudaErrorInvalidSymbol),
-                     "cudaGetSymbolAddress of the decode scratch array failed");
+  }
   *out = g_scratch_ptr[dev];
   return MI_OK;
 }
@@ -128,11 +134,17 @@ extern "C" int mi_paged_decode_noalloc(void *out, const void *query, const void 
   int dev = 0;
   cudaGetDevice(&dev);
   const int64_t ctx_bound = block_table_stride * block_size;
-  const int nsplit =
-      num_splits == 0 ? mi_paged_decode_default_splits(
-                            num_seqs, num_kv_heads,
-                            static_cast<int32_t>(ctx_bound > INT32_MAX ? INT32_MAX : ctx_bound), dev)
-                      : num_splits;
+  int nsplit = num_splits;
+  if (nsplit == 0) {
+    nsplit = mi_paged_decode_default_splits(
+        num_seqs, num_kv_heads, static_cast<int32_t>(ctx_bound > INT32_MAX ? INT32_MAX : ctx_bound),
+        dev);
+    // Cap the default to the split states the scratch holds.
+    const int64_t per_split = num_seqs * num_q_heads * (static_cast<int64_t>(head_dim) + 2) *
+                              static_cast<int64_t>(sizeof(float));
+    const int64_t fit = (static_cast<int64_t>(kNoAllocScratchBytes) - kSplitCounterBytes) / per_split;
+    if (nsplit > fit) nsplit = fit > 1 ? static_cast<int>(fit) : 1;
+  }
   DecodeParams p = {};
   p.out = out;
   p.query = query;

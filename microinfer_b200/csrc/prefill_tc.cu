@@ -1,35 +1,17 @@
 // tcgen05 (UMMA + TMEM) paged chunked-prefill attention for sm_100a.
 //
-// Work tile: 128 query rows = (TQ = 128/G tokens) x (G query heads of one kv
-// head), against every cached key of the sequence up to the tile's last
-// position, in 128-key tiles.  One CTA per (query tile, kv head, sequence);
-// 352 threads in four roles:
-//
-//   warps 0,10  TMA producers: warp 0 Q once (two 64-column halves, 3-D map
-//               over [tokens, Hq, D]) and the K tiles, warp 10 the V tiles: per
-//               key tile 8 groups of 16 keys (3-D map over [slots, Hkv, D]);
-//               each group's slot comes from the block table (looked up in
-//               batches of 4 tiles, one batch ahead), groups past the context
-//               load from an out-of-range
-//               coordinate (zero fill).  K ring of 3 stages, V ring of 2.
-//   warp 1      TMEM owner and single-thread MMA issuer:
-//                 S[j%2] = Q K_j^T   (M=128, N=128, K=D; A, B K-major)
-//                 O     += P_j V_j   (M=128, N=D,   K=128; B MN-major)
-//               S is double-buffered so S_{j+1} overlaps the softmax of S_j.
-//   warps 2-9   softmax, two warpgroups: TMEM lane (= query row) per thread,
-//               warps 2-5 columns 0-63 and warps 6-9 columns 64-127 of the
-//               row; read S with tcgen05.ld, causal mask only on diagonal
-//               tiles, online softmax in the log2 domain (scale folded into
-//               the FFMA feeding ex2) with lazy rescale of O (only when the
-//               row max grows by more than 2^8); the row halves combine their
-//               maxima through TMEM columns 384-387 at one barrier per tile;
-//               P as fp16/bf16 into the
-//               128-byte-swizzled shared tile the next MMA reads; epilogue
-//               O / l -> global.
+// Work unit: a pair of 128-row query tiles (each TQ = 128/G tokens x the G
+// query heads of one kv head) against every cached key of the sequence up to
+// the tile's last position, in 128-key tiles; K/V tiles are shared by both
+// query tiles.  Roles, TMEM layout and the MMA order are described above
+// prefill_tc2_kernel.
 //
 // Shared memory operands use the SWIZZLE_128B canonical layout (8 rows x 128
-// bytes atoms); a 128x128 16-bit tile is two 16 KB column halves.  TMEM: S0
-// at column 0, S1 at 128, O at 256, softmax exchange at 384 (512 allocated).
+// bytes atoms); a 128x128 16-bit tile is two 16 KB column halves.  K/V groups
+// of 16 keys come from a 3-D tensor map over [slots, Hkv, D]; each group's
+// slot comes from the block table, groups past the context load from an
+// out-of-range coordinate (zero fill), and the rows past the context inside
+// the last, partial group are zeroed in shared memory before P.V reads them.
 //
 // Dense mode (no block table) reads K/V rows cu_seqlens_k[s] + key of a
 // contiguous [tokens, Hkv, D] tensor: the no-prefix ("direct") prefill.
@@ -81,33 +63,12 @@ struct __align__(64) PrefillTcParams {
 
 namespace {
 
-constexpr int kThreads = 352;
 constexpr int kTileBytes = 32768;  // 128 x 128 x 16-bit
 constexpr int kHalf = 16384;
-constexpr int kOffQ = 0;
 constexpr int kKStages = 3;  // K is released after S (early), so it runs deeper than V
 constexpr int kVStages = 2;
-constexpr int kOffK = kOffQ + kTileBytes;
-constexpr int kOffV = kOffK + kKStages * kTileBytes;
-constexpr int kOffP = kOffV + kVStages * kTileBytes;
-constexpr int kOffBar = kOffP + kTileBytes;
-constexpr int kSmemBytes = kOffBar + 256 + 1024;  // barriers + TMEM slot + alignment slack
 constexpr uint32_t kTmemCols = 512;
 
-// barrier indices
-enum {
-  B_Q = 0,
-  B_KFULL = 1,    // +K stage (3)
-  B_VFULL = 4,    // +V stage (2)
-  B_KEMPTY = 6,   // +K stage
-  B_VEMPTY = 9,   // +V stage
-  B_SFULL = 11,   // +S buffer (2)
-  B_SEMPTY = 13,  // +S buffer
-  B_PFULL = 15,   // +tile parity
-  B_ODONE = 17,   // +tile parity: P.V of the tiles with that parity done
-  B_FIN = 19,
-  B_COUNT = 20
-};
 
 // K-major SW128 descriptor of 16-element K-step `kk` of a 128 x 128 tile.
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, int kk) {
@@ -127,384 +88,7 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   return *reinterpret_cast<uint32_t *>(&h);
 }
 
-// Barrier over the 8 softmax warps (id 1, 256 threads) that also ORs `bad`,
-// so every softmax warp takes the same exit.
-__device__ __forceinline__ bool softmax_pair_sync_any(bool bad) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred pin, pout;\n\tsetp.ne.u32 pin, %1, 0;\n\t"
-      "bar.red.or.pred pout, 1, 256, pin;\n\tselp.u32 %0, 1, 0, pout;\n\t}"
-      : "=r"(r)
-      : "r"(bad ? 1u : 0u)
-      : "memory");
-  return r != 0;
-}
-
 }  // namespace
-
-template <typename T, int G>
-__global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const __grid_constant__ PrefillTcParams p) {
-  constexpr int TQ = 128 / G;  // tokens per tile
-  constexpr bool kBf16 = sizeof(T) == 2 && Elem<T>::kDtype == MI_DTYPE_BFLOAT16;
-  constexpr uint32_t kIdescQK = tc::idesc_f16(128, 128, kBf16 ? 1 : 0, false);
-  constexpr uint32_t kIdescPV = tc::idesc_f16(128, 128, kBf16 ? 1 : 0, true);
-
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                              ~static_cast<uintptr_t>(1023));
-  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + kOffBar);
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bar + B_COUNT);
-  int *abort_flag = reinterpret_cast<int *>(tmem_slot + 1);
-  const uint32_t sQ = smem_addr(smem + kOffQ);
-  const uint32_t sK = smem_addr(smem + kOffK);
-  const uint32_t sV = smem_addr(smem + kOffV);
-  const uint32_t sP = smem_addr(smem + kOffP);
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, kvh = blockIdx.y;
-  const int64_t seq = blockIdx.z;
-
-  pdl_wait();
-  if (p.skip_single) pdl_launch_dependents();
-  const int q_start = p.cu_q[seq];
-  const int q_len = p.cu_q[seq + 1] - q_start;
-  const int t0 = qt * TQ;
-  if (t0 >= q_len) return;  // uniform: this sequence has fewer query tiles
-  if (p.skip_single && q_len == 1) return;  // a decode row: the decode launch handles it
-  const int kv0 = p.cu_k[seq];
-  const int ctx = p.cu_k[seq + 1] - kv0;
-  const int prefix = ctx - q_len;
-  const int nt = min(TQ, q_len - t0);
-  const int maxpos = prefix + t0 + nt - 1;
-  const int nkv = maxpos >= 0 ? maxpos / 128 + 1 : 0;
-  T *out = static_cast<T *>(p.out);
-  if (nkv == 0) {  // no visible key (context shorter than the chunk): zeros, as the generic kernel
-    for (int i = threadIdx.x; i < nt * G * 128; i += kThreads) {
-      const int row = i / 128, d = i % 128;
-      out[(static_cast<int64_t>(q_start + t0 + row / G) * p.num_q_heads + kvh * G + row % G) * 128 + d] =
-          Elem<T>::from_float(0.f);
-    }
-    return;
-  }
-
-  if (threadIdx.x == 0) {
-    mbar_init(&bar[B_Q], 1);
-    for (int s = 0; s < kKStages; ++s) {
-      mbar_init(&bar[B_KFULL + s], 1);
-      mbar_init(&bar[B_KEMPTY + s], 1);
-    }
-    for (int s = 0; s < kVStages; ++s) {
-      mbar_init(&bar[B_VFULL + s], 1);
-      mbar_init(&bar[B_VEMPTY + s], 1);
-    }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&bar[B_SFULL + s], 1);
-      mbar_init(&bar[B_SEMPTY + s], 256);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&bar[B_PFULL + b], 256);
-      mbar_init(&bar[B_ODONE + b], 1);
-    }
-    mbar_init(&bar[B_FIN], 1);
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 1) tc::tmem_alloc(tmem_slot, kTmemCols);
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + 256;
-
-  if (warp == 0 || warp == 10) {
-    // ---------------------------------------------------------- producers
-    // warp 0 loads Q and the K tiles, warp 10 the V tiles, so a K load never
-    // waits behind the (later) release of a V stage.  Each warp looks up the
-    // next tile's pages while it waits for the current stage.
-    const bool is_v = warp == 10;
-    const int32_t *table = p.block_tables + seq * p.bt_stride;
-    // Raw table entry for a 16-key group (loads only, so several can be in
-    // flight); validated and turned into a row when the group is loaded.
-    auto kv_entry = [&](int key0) -> int {
-      if (key0 >= ctx || !p.paged) return 0;
-      const int64_t col = key0 / p.block_size;
-      return col < p.bt_stride ? __ldg(table + col) : -1;
-    };
-    auto kv_row = [&](int key0, int entry) -> int {
-      if (key0 >= ctx) return static_cast<int>(p.kv_rows);  // past the context: zero fill
-      if (!p.paged) return kv0 + key0;
-      if (entry < 0 || entry >= p.num_blocks) {
-        flag_status(p.status, MI_DEV_BAD_BLOCK);
-        return static_cast<int>(p.kv_rows);
-      }
-      return static_cast<int>(static_cast<int64_t>(entry) * p.block_size + key0 % p.block_size);
-    };
-    bool ok = true;
-    int armed = 0;  // key tiles whose loads were issued
-    if (lane == 0) {
-      tc::prefetch_tmap(is_v ? &p.tmap_v : &p.tmap_k);
-      if (!is_v) {
-        tc::prefetch_tmap(&p.tmap_q);
-        mbar_arrive_expect_tx(&bar[B_Q], 2 * kHalf);
-        for (int dh = 0; dh < 2; ++dh)
-          tc::tma_load_3d(smem + kOffQ + dh * kHalf, &p.tmap_q, dh * 64, kvh * G, q_start + t0, &bar[B_Q]);
-      }
-    }
-    // lanes 0..15 each load one (16-key group, 64-column half) box
-    const int g = lane >> 1, dh = lane & 1;
-    const int nst = is_v ? kVStages : kKStages;
-    const CUtensorMap *map = is_v ? &p.tmap_v : &p.tmap_k;
-    uint8_t *ring = smem + (is_v ? kOffV : kOffK);
-    const int full0 = is_v ? B_VFULL : B_KFULL, empty0 = is_v ? B_VEMPTY : B_KEMPTY;
-    // Page lookups in batches of 4 tiles: lane (t, b) of the warp holds the
-    // table entry of group b of tile 4k + t; the next batch is loaded a whole
-    // batch ahead, and a shuffle hands each copy lane its entry, so no
-    // register move ever waits on a recent load.
-    const int bt = lane >> 3, bg = lane & 7;
-    auto entry_for = [&](int tile) { return tile < nkv ? kv_entry(tile * 128 + bg * 16) : 0; };
-    int cur = entry_for(bt), nxt = entry_for(4 + bt);
-    for (int j = 0; j < nkv && ok; ++j) {
-      const int s = j % nst;
-      const uint32_t empty_parity = ((j / nst) & 1) ^ 1;
-      if (j > 0 && (j & 3) == 0) {
-        cur = nxt;
-        nxt = entry_for(j + 4 + bt);
-      }
-      const int entry = __shfl_sync(0xffffffffu, cur, ((j & 3) * 8 + g) & 31);
-      const int row = lane < 16 ? kv_row(j * 128 + g * 16, entry) : 0;
-      int good = 1;
-      if (lane == 0) good = mbar_wait_bounded(&bar[empty0 + s], empty_parity, p.status) && !*(volatile int *)abort_flag;
-      good = __shfl_sync(0xffffffffu, good, 0);
-      if (!good) {
-        ok = false;
-        break;
-      }
-      if (lane == 0) mbar_arrive_expect_tx(&bar[full0 + s], kTileBytes);
-      __syncwarp();
-      if (lane < 16)
-        tc::tma_load_3d(ring + s * kTileBytes + dh * kHalf + g * 2048, map, dh * 64, kvh, row, &bar[full0 + s]);
-      armed = j + 1;
-    }
-    if (!ok) {
-      if (lane == 0) *(volatile int *)abort_flag = 1;
-      // Let this CTA's own loads in flight land before its shared memory goes away.
-      if (lane == 0)
-        for (int j = max(0, armed - nst); j < armed; ++j)
-          mbar_wait_bounded(&bar[full0 + j % nst], (j / nst) & 1, p.status);
-    }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      bool ok = mbar_wait_bounded(&bar[B_Q], 0, p.status);
-      auto pv = [&](int jj) -> bool {
-        const int s = jj & 1;  // V stage and P buffer
-        if (!mbar_wait_bounded(&bar[B_PFULL + s], (jj >> 1) & 1, p.status)) return false;
-        if (!mbar_wait_bounded(&bar[B_VFULL + s], (jj >> 1) & 1, p.status)) return false;
-        tc::fence_after_sync();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          tc::umma_f16(tO, kmajor_desc(sP, kk), mnmajor_desc(sV + s * kTileBytes, kk), kIdescPV,
-                       (jj > 0 || kk > 0) ? 1u : 0u);
-        tc::umma_commit(&bar[B_ODONE + s]);
-        tc::umma_commit(&bar[B_VEMPTY + s]);
-        return true;
-      };
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j & 1, ks = j % kKStages;
-        ok = mbar_wait_bounded(&bar[B_KFULL + ks], (j / kKStages) & 1, p.status) &&
-             mbar_wait_bounded(&bar[B_SEMPTY + s], ((j >> 1) & 1) ^ 1, p.status) &&
-             !*(volatile int *)abort_flag;
-        if (!ok) break;
-        tc::fence_after_sync();
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          tc::umma_f16(tS + s * 128, kmajor_desc(sQ, kk), kmajor_desc(sK + ks * kTileBytes, kk),
-                       kIdescQK, kk > 0 ? 1u : 0u);
-        tc::umma_commit(&bar[B_SFULL + s]);
-        tc::umma_commit(&bar[B_KEMPTY + ks]);
-        if (j >= 1) ok = pv(j - 1);
-      }
-      if (ok) ok = pv(nkv - 1);
-      if (!ok) *(volatile int *)abort_flag = 1;
-      // Every MMA issued by this thread completes before TMEM is released.
-      tc::umma_commit(&bar[B_FIN]);
-      mbar_wait_bounded(&bar[B_FIN], 0, p.status);
-    }
-    __syncwarp();
-  } else {
-    // ------------------------------------------------------------ softmax
-    // Two warpgroups: warps 2-5 take columns 0-63 of every row, warps 6-9
-    // columns 64-127 (a warp reaches the TMEM lanes 32 * (warp % 4) ...).  The
-    // two halves of a row exchange their partial max once per tile through
-    // shared memory at a 256-thread barrier that also ORs an abort flag.
-    const int q4 = warp & 3;
-    const int hc = warp >= 6 ? 1 : 0;  // column half
-    const int r = q4 * 32 + lane;      // TMEM lane = query row of the tile
-    const int tok = r / G;
-    const bool rvalid = tok < nt;
-    const int pos = prefix + t0 + tok;
-    const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
-    uint8_t *prow = smem + kOffP + hc * kHalf + r * 128;
-    // Exchange slots in TMEM columns 384 + 2 * parity + half (lane = row).
-    const uint32_t tX = tmem + 384 + lane_off;
-    const float sl2 = p.scale_log2;
-    const bool pos_scale = sl2 >= 0.f;
-    float m = -INFINITY, l = 0.f;  // l: this half's share of the row sum
-    bool ok = true, bad = false;
-    for (int j = 0; j < nkv; ++j) {
-      const int s = j & 1;
-      const bool got = mbar_wait_bounded(&bar[B_SFULL + s], (j >> 1) & 1, p.status) &&
-                       !*(volatile int *)abort_flag;
-      float x[64];
-      if (got) {
-        tc::fence_after_sync();
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float v[32];
-          tc::tmem_ld32(tS + s * 128 + hc * 64 + lane_off + c * 32, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) x[c * 32 + i] = v[i];
-        }
-        tc::tmem_wait_ld();
-        tc::fence_before_sync();
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) x[i] = 0.f;
-      }
-      mbar_arrive(&bar[B_SEMPTY + s]);
-      bad |= !got;
-
-      // key c of this half is visible iff hc * 64 + c <= pos - j * 128
-      const int lim = rvalid ? pos - j * 128 - hc * 64 : -1;
-      if (lim < 63) {
-        const float masked = pos_scale ? -INFINITY : INFINITY;
-#pragma unroll
-        for (int c = 0; c < 64; ++c) x[c] = c <= lim ? x[c] : masked;
-      }
-      float r4[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) r4[i] = pos_scale ? -INFINITY : INFINITY;
-      if (pos_scale) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) r4[c & 3] = fmaxf(r4[c & 3], x[c]);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) r4[c & 3] = fminf(r4[c & 3], x[c]);
-      }
-      const float best = pos_scale ? fmaxf(fmaxf(r4[0], r4[1]), fmaxf(r4[2], r4[3]))
-                                   : fminf(fminf(r4[0], r4[1]), fminf(r4[2], r4[3]));
-      const float hmx = lim < 0 ? -INFINITY : best * sl2;  // this half's max, log2 domain
-      tc::tmem_st1(tX + s * 2 + hc, hmx);
-      tc::tmem_wait_st();
-      tc::fence_before_sync();
-      if (softmax_pair_sync_any(bad)) {  // also publishes the halves' maxima
-        ok = false;
-        break;
-      }
-      tc::fence_after_sync();
-      const float other = tc::tmem_ld1(tX + s * 2 + (hc ^ 1));
-      tc::tmem_wait_ld();
-      const float mx = fmaxf(hmx, other);
-      float m_new = m, alpha = 1.f;
-      bool rescale = false;
-      if (mx > m + 8.f) {
-        m_new = mx;
-        rescale = m != -INFINITY;
-        alpha = rescale ? fast_exp2(m - m_new) : 0.f;
-      }
-      // Exponentials first (packed to 16-bit pairs in registers), while the
-      // tensor core may still be running P.V(j-1).
-      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
-      const float nb = m_new == -INFINITY ? 0.f : -m_new;  // masked: ex2(-inf) = 0
-      uint32_t pk[32];
-#pragma unroll
-      for (int c2 = 0; c2 < 32; ++c2) {
-        const float e0 = fast_exp2(fmaf(x[2 * c2], sl2, nb));
-        const float e1 = fast_exp2(fmaf(x[2 * c2 + 1], sl2, nb));
-        rs4[(2 * c2) & 3] += e0;
-        rs4[(2 * c2 + 1) & 3] += e1;
-        pk[c2] = pack2(e0, e1, kBf16);
-      }
-      // The single P buffer and O are free once P.V(j-1) is done.
-      if (j >= 1) {
-        const bool done = mbar_wait_bounded(&bar[B_ODONE + ((j - 1) & 1)], ((j - 1) >> 1) & 1,
-                                            p.status);
-        bad |= !done;  // acted on at the next barrier; the writes below stay in bounds
-        tc::fence_after_sync();
-        if (__any_sync(0xffffffffu, rescale)) {
-          const float a = rescale ? alpha : 1.f;
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            float o[32];
-            tc::tmem_ld32(tO + hc * 64 + lane_off + c * 32, o);
-            tc::tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= a;
-            tc::tmem_st32(tO + hc * 64 + lane_off + c * 32, o);
-          }
-          tc::tmem_wait_st();
-        }
-      }
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8)
-        *reinterpret_cast<uint4 *>(prow + ((c8 ^ (r & 7)) << 4)) =
-            make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
-      l = l * alpha + ((rs4[0] + rs4[1]) + (rs4[2] + rs4[3]));
-      m = m_new;
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
-      tc::fence_before_sync();
-      mbar_arrive(&bar[B_PFULL + s]);
-    }
-    // Row sum of both halves; the barrier also settles a pending abort.
-    if (ok) {
-      tc::tmem_st1(tX + (nkv & 1) * 2 + hc, l);
-      tc::tmem_wait_st();
-      tc::fence_before_sync();
-      ok = !softmax_pair_sync_any(bad);
-    }
-    float L = 0.f;
-    if (ok) {
-      tc::fence_after_sync();
-      L = l + tc::tmem_ld1(tX + (nkv & 1) * 2 + (hc ^ 1));
-      tc::tmem_wait_ld();
-      const int good = mbar_wait_bounded(&bar[B_ODONE + ((nkv - 1) & 1)], ((nkv - 1) >> 1) & 1, p.status);
-      ok = __all_sync(0xffffffffu, good);
-    }
-    if (ok) {
-      tc::fence_after_sync();
-      const float inv = L > 0.f ? 1.f / L : 0.f;
-      T *orow = out + (static_cast<int64_t>(q_start + t0 + tok) * p.num_q_heads + kvh * G + r % G) * 128 +
-                hc * 64;
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float o[32];
-        tc::tmem_ld32(tO + hc * 64 + lane_off + c * 32, o);
-        tc::tmem_wait_ld();
-        if (rvalid) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 w;
-            w.x = pack2(o[i] * inv, o[i + 1] * inv, kBf16);
-            w.y = pack2(o[i + 2] * inv, o[i + 3] * inv, kBf16);
-            w.z = pack2(o[i + 4] * inv, o[i + 5] * inv, kBf16);
-            w.w = pack2(o[i + 6] * inv, o[i + 7] * inv, kBf16);
-            *reinterpret_cast<uint4 *>(orow + c * 32 + i) = w;
-          }
-        }
-      }
-    } else if (lane == 0) {
-      *(volatile int *)abort_flag = 1;
-    }
-  }
-
-  pdl_launch_dependents();
-  tc::fence_before_sync();
-  __syncthreads();
-  if (warp == 1) {
-    tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, kTmemCols);
-  }
-}
 
 // ---------------------------------------------------------------------------
 // Two query tiles per CTA (prefill_tc2_kernel).
@@ -545,7 +129,8 @@ enum {
   C_PFULL = 13,  // +tile: P_X(j) in TMEM (128 softmax threads)
   C_ODONE = 15,  // every MMA done
   C_FIN = 16,
-  C_COUNT = 17
+  C_VFIX = 17,   // rows past the context in the last V group zeroed (32 lanes of warp 10)
+  C_COUNT = 18
 };
 
 // Warp-uniform: this lane's wait succeeded in every lane and nobody aborted.
@@ -600,6 +185,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
     nkv_t[x] = nt[x] > 0 && maxpos >= 0 ? maxpos / 128 + 1 : 0;
   }
   const int nkv = max(nkv_t[0], nkv_t[1]);
+  // The last key tile may hold a partial 16-key group (rows ctx % 16 .. 15 of
+  // it lie past the context and hold stale pool contents, or another
+  // sequence's rows in dense mode).  They meet P = 0, but 0 * Inf or NaN is
+  // NaN, so the V producer zeroes them before P.V reads that tile.
+  const int fix_tile = (ctx % 16 != 0 && (ctx - 1) / 128 == nkv - 1) ? nkv - 1 : -1;
+  const int fix_group = ((ctx - 1) % 128) / 16, fix_valid = ctx % 16;
   T *out = static_cast<T *>(p.out);
   if (nkv == 0) {  // no visible key (context shorter than the chunk): zeros, as the generic kernel
     for (int i = threadIdx.x; i < (nt[0] + nt[1]) * G * 128; i += kThreads2) {
@@ -626,6 +217,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
     }
     mbar_init(&bar[C_ODONE], 1);
     mbar_init(&bar[C_FIN], 1);
+    mbar_init(&bar[C_VFIX], 32);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -699,6 +291,26 @@ __global__ void __launch_bounds__(kThreads2, 1)
       if (lane < 16)
         tc::tma_load_3d(ring + s * kTileBytes + dh * kHalf + g * 2048, map, dh * 64, kvh, row, &bar[full0 + s]);
       armed = j + 1;
+      if (is_v && j == fix_tile) {
+        // Wait for the tile, zero the group's rows past the context (both 64-column
+        // halves; whole 128-byte rows, so the swizzle does not matter), make the
+        // writes visible to the tensor core and release the tile to the MMA issuer.
+        int landed = 1;
+        if (lane == 0) landed = mbar_wait_bounded(&bar[full0 + s], (j / nst) & 1, p.status);
+        landed = __shfl_sync(0xffffffffu, landed, 0);
+        if (landed) {
+          uint8_t *grp = ring + s * kTileBytes + fix_group * 2048;
+          for (int i = lane; i < (16 - fix_valid) * 16; i += 32) {
+            const int rr = fix_valid + i / 16, c = i % 16;
+            *reinterpret_cast<uint4 *>(grp + (c >> 3) * kHalf + rr * 128 + (c & 7) * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
+        } else {
+          ok = false;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&bar[C_VFIX]);
+      }
     }
     if (!ok && lane == 0) {
       *(volatile int *)abort_flag = 1;
@@ -741,6 +353,7 @@ __global__ void __launch_bounds__(kThreads2, 1)
         ok = mbar_spin_bounded(&bar[C_VFULL + vs], (j / kVStages) & 1, p.status) &&
              (!(nA || nB) || mbar_spin_bounded(&bar[C_KFULL + ks], ((j + 1) / kKStages) & 1, p.status)) &&
              !*(volatile int *)abort_flag;
+        if (ok && j == fix_tile) ok = mbar_spin_bounded(&bar[C_VFIX], 0, p.status);
         if (!ok) break;
         tc::fence_after_sync();
         if (j < nkv_t[0] && !(ok = pv_mma(0, j))) break;
@@ -906,23 +519,6 @@ bool encode_3d(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint6
 }
 
 template <typename T, int G>
-cudaError_t launch_tg(PrefillTcParams &p, int num_kv_heads, int64_t num_seqs, int32_t max_seqlen_q,
-                      cudaStream_t stream) {
-  auto kern = prefill_tc_kernel<T, G>;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
-  constexpr int TQ = 128 / G;
-  const dim3 grid((max_seqlen_q + TQ - 1) / TQ, num_kv_heads, static_cast<unsigned>(num_seqs));
-  return launch_pdl(kern, grid, dim3(kThreads), kSmemBytes, stream, p);
-}
-
-template <typename T, int G>
 cudaError_t launch_tg2(PrefillTcParams &p, int num_kv_heads, int64_t num_seqs, int32_t max_seqlen_q,
                        cudaStream_t stream) {
   auto kern = prefill_tc2_kernel<T, G>;
@@ -945,23 +541,6 @@ cudaError_t launch_tg2(PrefillTcParams &p, int num_kv_heads, int64_t num_seqs, i
   p.num_kv_heads = num_kv_heads;
   p.split_from = units - split;
   return launch_pdl(kern, dim3(static_cast<unsigned>(units + split)), dim3(kThreads2), kSmemBytes2, stream, p);
-}
-
-// Two query tiles per CTA unless MICROINFER_B200_PREFILL=tc1 pins the
-// one-tile kernel.
-bool prefill_two_tiles() {
-  static const bool two = [] {
-    const char *v = std::getenv("MICROINFER_B200_PREFILL");
-    return !(v != nullptr && std::strcmp(v, "tc1") == 0);
-  }();
-  return two;
-}
-
-template <typename T, int G>
-cudaError_t launch_any(PrefillTcParams &p, int num_kv_heads, int64_t num_seqs, int32_t max_seqlen_q,
-                       cudaStream_t stream) {
-  return prefill_two_tiles() ? launch_tg2<T, G>(p, num_kv_heads, num_seqs, max_seqlen_q, stream)
-                             : launch_tg<T, G>(p, num_kv_heads, num_seqs, max_seqlen_q, stream);
 }
 
 }  // namespace
@@ -1015,17 +594,17 @@ cudaError_t launch_prefill_tc(const AttnParams &a, int dtype, int G, int32_t max
   const int64_t n = a.num_seqs;
   if (dtype == MI_DTYPE_BFLOAT16) {
     switch (G) {
-      case 1: return launch_any<__nv_bfloat16, 1>(p, a.num_kv_heads, n, max_seqlen_q, stream);
-      case 2: return launch_any<__nv_bfloat16, 2>(p, a.num_kv_heads, n, max_seqlen_q, stream);
-      case 4: return launch_any<__nv_bfloat16, 4>(p, a.num_kv_heads, n, max_seqlen_q, stream);
-      default: return launch_any<__nv_bfloat16, 8>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+      case 1: return launch_tg2<__nv_bfloat16, 1>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+      case 2: return launch_tg2<__nv_bfloat16, 2>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+      case 4: return launch_tg2<__nv_bfloat16, 4>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+      default: return launch_tg2<__nv_bfloat16, 8>(p, a.num_kv_heads, n, max_seqlen_q, stream);
     }
   }
   switch (G) {
-    case 1: return launch_any<__half, 1>(p, a.num_kv_heads, n, max_seqlen_q, stream);
-    case 2: return launch_any<__half, 2>(p, a.num_kv_heads, n, max_seqlen_q, stream);
-    case 4: return launch_any<__half, 4>(p, a.num_kv_heads, n, max_seqlen_q, stream);
-    default: return launch_any<__half, 8>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+    case 1: return launch_tg2<__half, 1>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+    case 2: return launch_tg2<__half, 2>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+    case 4: return launch_tg2<__half, 4>(p, a.num_kv_heads, n, max_seqlen_q, stream);
+    default: return launch_tg2<__half, 8>(p, a.num_kv_heads, n, max_seqlen_q, stream);
   }
 }
 

@@ -87,7 +87,7 @@ def select_split_k(num_requests: int, num_kv_heads: int, device=None,
     return _lib.load().mi_paged_decode_default_splits(num_requests, num_kv_heads, max_context, dev)
 
 
-DECODE_KERNELS = {1: "generic", 2: "simt", 3: "tcgen05", 4: "mma"}
+DECODE_KERNELS = {1: "generic", 2: "simt", 4: "mma"}
 
 
 def decode_plan(num_requests: int, num_q_heads: int, num_kv_heads: int, head_dim: int,

@@ -594,3 +594,67 @@ def test_mma_decode_shapes_match_oracle(dtype, d, g, bs, split, fused):
     expected = po.paged_decode(host(q, dtype), host(kc, dtype), host(vc, dtype), table.numpy(),
                                ctx.numpy(), scale=scale, dtype=dtype)
     assert_close(out, expected, dtype)
+
+
+@pytest.mark.parametrize("poison", [float("inf"), float("nan"), -float("inf")])
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_non_finite_rows_past_the_context_never_reach_the_output(poison, dtype, cuda_device):
+    """Pool rows past each context (inside its last, partial page, and the rest of the
+    pool) hold Inf or NaN, as a freed page reused after an overflow could.  The reference
+    slices exactly `ctx` rows, so its output stays finite; the tcgen05 prefill (multi-token
+    chunks, partial 16-key groups at the end of every context), the mma decode and the dense
+    prefill must too.  Rows within the contexts are finite random values."""
+    torch_dt = TORCH[dtype]
+    hq, hkv, d, bs = 16, 8, 128, 16
+    q_lens, contexts = [150, 37, 1, 129], [173, 37, 301, 500]
+    need = [(c + bs - 1) // bs for c in contexts]
+    nb = sum(need) + 2
+    g = torch.Generator(device="cpu").manual_seed(41)
+    table = torch.full((len(contexts), max(need)), -1, dtype=torch.int32)
+    perm = torch.randperm(nb, generator=g).to(torch.int32)
+    at = 0
+    for r, k in enumerate(need):
+        table[r, :k] = perm[at:at + k]
+        at += k
+    kc = torch.full((nb, bs, hkv, d), poison, dtype=torch.float32)
+    vc = torch.full_like(kc, poison)
+    for r, c in enumerate(contexts):  # finite rows only inside the contexts
+        for pos in range(c):
+            blk, off = int(table[r, pos // bs]), pos % bs
+            kc[blk, off] = torch.randn(hkv, d, generator=g)
+            vc[blk, off] = torch.randn(hkv, d, generator=g)
+    kc, vc = kc.to(torch_dt).to(cuda_device), vc.to(torch_dt).to(cuda_device)
+    total = sum(q_lens)
+    q = torch.randn(total, hq, d, generator=g).to(torch_dt).to(cuda_device)
+    cu_q = torch.tensor([0] + np.cumsum(q_lens).tolist(), dtype=torch.int32)
+    cu_k = torch.tensor([0] + np.cumsum(contexts).tolist(), dtype=torch.int32)
+    out = mi.paged_prefill(q, kc, vc, cu_q.to(cuda_device), cu_k.to(cuda_device),
+                           table.to(cuda_device), max_seqlen_q=max(q_lens))
+    assert torch.isfinite(out.float()).all(), "prefill read a non-finite row past a context"
+    expected = po.paged_attention(host(q, dtype), host(kc, dtype), host(vc, dtype),
+                                  table.numpy(), contexts, cu_q.numpy(), scale=1 / math.sqrt(d),
+                                  dtype=dtype)
+    assert_close(out, expected, dtype)
+    # decode over the same pool (one query per sequence), with and without splits
+    qd = torch.randn(len(contexts), hq, d, generator=g).to(torch_dt).to(cuda_device)
+    ctx_d = torch.tensor(contexts, dtype=torch.int32, device=cuda_device)
+    exp_d = po.paged_decode(host(qd, dtype), host(kc, dtype), host(vc, dtype), table.numpy(),
+                            contexts, scale=1 / math.sqrt(d), dtype=dtype)
+    for split in (1, 3):
+        outd = mi.paged_decode(qd, kc, vc, table.to(cuda_device), ctx_d, split_k=split)
+        assert torch.isfinite(outd.float()).all()
+        assert_close(outd, exp_d, dtype)
+    # dense (no-prefix) prefill whose last sequence ends inside a 16-row group and is
+    # followed by non-finite rows of the packed tensor
+    lens = [40, 21]
+    kd = torch.randn(64, hkv, d, generator=g).to(torch_dt)
+    vd = torch.randn(64, hkv, d, generator=g).to(torch_dt)
+    kd[61:], vd[61:] = poison, poison
+    qd2 = torch.randn(61, hq, d, generator=g).to(torch_dt)
+    cu = torch.tensor([0, 40, 61], dtype=torch.int32)
+    outv = mi.varlen_prefill(qd2.to(cuda_device), kd.to(cuda_device), vd.to(cuda_device),
+                             cu.to(cuda_device), cu.to(cuda_device), max_seqlen_q=max(lens))
+    assert torch.isfinite(outv.float()).all()
+    exp_v = po.dense_varlen_attention(host(qd2, dtype), host(kd[:61], dtype), host(vd[:61], dtype),
+                                      cu.numpy(), scale=1 / math.sqrt(d), dtype=dtype)
+    assert_close(outv, exp_v, dtype)
