@@ -47,6 +47,7 @@ WORKLOAD = "BASELINE configs[1]: Qwen3-0.6B decode step, bf16, 28 layers, batch 
 
 # kernel names for the roofline entry and the ncu summaries that measured them
 DECODE_KERNEL_NAMES = {"mma": "paged_decode_mma_kernel", "simt": "paged_decode_kernel",
+                       "mma_pair": "paged_decode_mma_kernel (cluster pairs)",
                        "generic": "attn_generic_kernel"}
 DECODE_PROFILES = {"mma": "decode_mma_qwen3_0.6b_config2.md"}
 
@@ -88,7 +89,7 @@ def make_batch(seed: int, device):
 
 
 def algorithmic_bytes(ctx_list):
-    from oracle.paged_oracle import decode_bytes, store_bytes
+    from tests.golden.configs import decode_bytes, store_bytes
 
     dec = decode_bytes(ctx_list, HQ, HKV, D, 2, BS)
     st = store_bytes(len(ctx_list), HKV, D, 2)
@@ -151,6 +152,67 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
                 "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
                 "samples": len(self.samples), "source": "nvml" if self._nv else "unavailable"}
+
+
+def bench_config(world: int) -> dict:
+    """The workload's `config`, identical in both arms."""
+    return {"workload": WORKLOAD, "global_batch": NSEQ * world, "per_gpu_batch": NSEQ,
+            "context": [CTX_LO, CTX_HI], "layers": LAYERS, "block_size": BS,
+            "num_blocks_per_layer": NB, "heads": [HQ, HKV], "head_dim": D,
+            "parallelism": f"sequence-sharded x{world}",
+            "l2": "inputs larger than L2: 28 distinct layer pools (1.88 GB) per GPU"}
+
+
+def reference_cpu_baseline(seconds: float = 12.0, pools: int = 4):
+    """The reference's own CPU implementation of the step, unmodified, from its
+    pip install under baseline/_ref: per layer `LayerKVCache.write_fast` (its
+    CPU branch, worker/kv_cache.py:52-79) then `_paged_attention_reference`
+    (layer/paged_attention.py:22-67), torch on every host core, over `pools`
+    distinct layer pools (0.27 GB, more than a CPU cache) for a bounded sample
+    of layers.  None when the install is absent."""
+    ref_dir = ROOT / "baseline" / "_ref"
+    if not (ref_dir / "microinfer").is_dir():
+        return None
+    if str(ref_dir) not in sys.path:
+        sys.path.insert(0, str(ref_dir))
+    import torch
+    from microinfer.layer.paged_attention import _paged_attention_reference
+    from microinfer.worker.kv_cache import LayerKVCache
+
+    from tests.golden.configs import decode_bytes, store_bytes
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ctx, table, slots = make_batch(1000, "cpu")
+    g = torch.Generator().manual_seed(0)
+    layers = [LayerKVCache((torch.randn(NB, BS, HKV, D, generator=g) * 0.5).to(torch.bfloat16),
+                           (torch.randn(NB, BS, HKV, D, generator=g) * 0.5).to(torch.bfloat16))
+              for _ in range(pools)]
+    q = torch.randn(NSEQ, HQ, D, generator=g).to(torch.bfloat16)
+    kn = torch.randn(NSEQ, HKV, D, generator=g).to(torch.bfloat16)
+    vn = torch.randn(NSEQ, HKV, D, generator=g).to(torch.bfloat16)
+    sl = slots.long()
+    blocks, offsets = sl // BS, sl % BS  # AttentionMetadata.slot_indices, once per step
+    ctx_list, cu_q = ctx.tolist(), list(range(NSEQ + 1))
+    step_b = decode_bytes(ctx_list, HQ, HKV, D, 2, BS) + store_bytes(NSEQ, HKV, D, 2)
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        layer = layers[done % pools]
+        layer.write_fast(blocks, offsets, kn, vn)
+        _paged_attention_reference(q, layer.keys, layer.values, table, ctx_list, cu_q,
+                                   scale=1 / math.sqrt(D))
+        done += 1
+        el = time.perf_counter() - t0
+        if el > seconds or done >= 20 * LAYERS:
+            break
+    return {"value": round(done * step_b / el / 1e9, 4), "unit": "GB/s", "cores": threads,
+            "kind": "reference",
+            "sample": f"{done} layer store+decode steps of the same workload through the "
+                      f"reference's own write_fast + _paged_attention_reference (baseline/_ref, "
+                      f"unmodified; torch CPU, {threads} threads, {pools} distinct layer pools), "
+                      f"{el:.1f} s",
+            "ms_per_28_layer_step": round(el / done * LAYERS * 1e3, 3)}
 
 
 def cpu_baseline(seconds: float = 12.0):
@@ -224,144 +286,168 @@ def measure_long_b1(device, reps: int = 20):
             # as in the config-2 step: layer i's decode writes neither layer i+1's pool
             # nor the table, so layer i+1's pages may load early
             mi.paged_decode_store(q[i], view.keys, view.values, table, ctx, kn[i], kn[i], slots,
-                                  split_k=split, out=out[i], early_kv=True)
+                                  split_k=None, out=out[i], early_kv=True)
 
     run()
     torch.cuda.synchronize(device)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        run()
-    for _ in range(3):
-        graph.replay()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize(device)
-    ms = e0.elapsed_time(e1) / reps
-    from oracle.paged_oracle import decode_bytes, store_bytes
+    mi.check_device_status(device)
+    cu = torch.tensor([0, 1], dtype=torch.int32)
+    check = _check_attention(out[-1], q[-1], views[-1].keys, views[-1].values,
+                             {"cu_q": cu, "table": table, "contexts": [ctx_len]}, [0],
+                             "configs[4] run (b)")
+    ms = _graph_ms(device, run, reps, warm=3)
+    from tests.golden.configs import decode_bytes, store_bytes
 
     b = layers * (decode_bytes([ctx_len], hq, hkv, D, 2, BS) + store_bytes(1, hkv, D, 2))
-    del graph, pool
+    del pool
     peaks, src = _peaks()
     gbs = b / (ms * 1e-3) / 1e9
     return {"workload": "BASELINE configs[4] run (b): batch 1, context 32768, 32q/8kv, D128, "
                         "36 layers, bs16", "kernel": kernel, "split_k": split,
             "ms_per_step": round(ms, 4),
             "value": round(gbs, 1), "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
-            "peak_source": f"hbm_gbs of {src}", "tok_per_s": round(1000.0 / ms, 1)}
+            "peak_source": f"hbm_gbs of {src}", "tok_per_s": round(1000.0 / ms, 1),
+            "checked": check}
 
 
-def measure_long_batch(device, layers: int = 36, pools: int = 4, reps: int = 3):
-    """BASELINE configs[4] run (a): 256 Qwen3-8B-shaped sequences, contexts
-    U[4096, 32768], 36 layers.
+ATOL, RTOL = 2e-2, 1e-2  # the parity tolerance (bf16, fp32 accumulation)
 
-    One layer's KV is ~19 GB, so the 36 layer launches cycle over `pools`
-    distinct layer pools (each far larger than L2) -- the per-GPU share of
-    the 8-GPU configuration.  Store + decode per layer, one CUDA graph.
-    """
+
+def _check_attention(out, q, kc, vc, b, rows, what):
+    """Whole requests `rows` of one timed layer against the reference's
+    `_paged_attention_reference` restated in fp32 on the device
+    (tests/golden/configs.py), before any timing.  Raises on a mismatch."""
     import torch
 
-    import microinfer_b200 as mi
-    from oracle.paged_oracle import decode_bytes, store_bytes
+    from tests.golden import configs
 
-    n, hq, hkv = 256, 32, 8
-    g = torch.Generator(device="cpu").manual_seed(7)
-    ctx = torch.randint(4096, 32769, (n,), generator=g, dtype=torch.int32)
-    need = [(int(c) + BS - 1) // BS for c in ctx]
-    nb = sum(need) + 1
-    table = torch.full((n, max(need)), -1, dtype=torch.int32)
-    perm = torch.randperm(nb, generator=g).to(torch.int32)
-    at = 0
-    for r, k in enumerate(need):
-        table[r, :k] = perm[at:at + k]
-        at += k
-    pos = (ctx - 1).long()
-    slots = (table[torch.arange(n), pos // BS].long() * BS + pos % BS).to(torch.int32)
+    cu = [int(x) for x in b["cu_q"].tolist()]
+    ref = configs.torch_paged_attention(q, kc, vc, b["table"], b["contexts"], cu,
+                                        1.0 / math.sqrt(q.shape[-1]), rows=rows)
+    worst = 0.0
+    for r in rows:
+        s, e = cu[r], cu[r + 1]
+        a, x = out[s:e].float(), ref[s:e].float()
+        err = (a - x).abs().max().item() if e > s else 0.0
+        if not bool(torch.isfinite(a).all()) or not torch.allclose(a, x, atol=ATOL, rtol=RTOL):
+            raise RuntimeError(f"{what}: request {r} differs from the reference restatement "
+                               f"(max abs err {err:.3g}); not timed")
+        worst = max(worst, err)
+    return {"requests_checked": len(rows), "max_abs_err": round(worst, 5),
+            "against": "fp32 restatement of _paged_attention_reference, 2e-2 abs / 1e-2 rel"}
+
+
+def _graph_ms(device, run, reps, warm=2):
+    """ms per replay of a CUDA graph of `run` (CUDA events on the replay stream)."""
+    import torch
+
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run()
+    for _ in range(warm):
+        graph.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream(device)
+    e0.record(cur)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(cur)
+    torch.cuda.synchronize(device)
+    del graph
+    return e0.elapsed_time(e1) / reps
+
+
+def measure_long_batch(device, world: int = 1, rank: int = 0, layers: int = 36, reps: int = 3,
+                       pool_budget_gb: float = 100.0):
+    """BASELINE configs[4] run (a): 256 Qwen3-8B-shaped sequences, contexts
+    U[4096, 32768], 36 layers, sharded by sequence over the ranks.
+
+    Every rank takes the sequences `sharding.assign_sequences` gives it
+    (balanced by total context, the decode bytes), owns its own pool and
+    block ids, and runs store + decode for its shard, 36 layers in one CUDA
+    graph; no collective is on the path.  One layer of the whole batch is
+    ~19 GB, so a rank holds as many distinct layer pools as fit in
+    `pool_budget_gb` (all 36 at 8 GPUs) and cycles the 36 layer launches over
+    them; every pool is far larger than L2.  Throughput = bytes of all 256
+    sequences x 36 layers / the slowest rank's time.
+    """
+    import torch
+    import torch.distributed as dist
+
+    import microinfer_b200 as mi
+    from microinfer_b200.sharding import assign_sequences
+    from tests.golden import configs
+    from tests.golden.configs import decode_bytes, store_bytes
+
+    hq, hkv = 32, 8
+    full = configs.long_batch(256)
+    shard = assign_sequences(full["contexts"], world)[rank]
+    contexts = [full["contexts"][i] for i in shard]
+    n = len(contexts)
+    gen = torch.Generator().manual_seed(70 + rank)
+    nb = sum((c + BS - 1) // BS for c in contexts) + 1
+    b = configs._finish([1] * n, contexts, configs._tables(gen, contexts, nb), nb)
+    layer_bytes = 2 * nb * BS * hkv * D * 2
+    pools = max(1, min(layers, int(pool_budget_gb * 1e9 // layer_bytes)))
     pool = mi.KVCache(pools, nb, BS, hkv, D, dtype=torch.bfloat16, device=device)
-    gd = torch.Generator(device=device).manual_seed(7)
+    gd = torch.Generator(device=device).manual_seed(7 + rank)
     pool.keys.normal_(generator=gd).mul_(0.5)
     pool.values.normal_(generator=gd).mul_(0.5)
-    ctx_d, table_d, slots_d = ctx.to(device), table.to(device), slots.to(device)
+    ctx_d = torch.tensor(contexts, dtype=torch.int32, device=device)
+    table_d, slots_d = b["table"].to(device), b["slots"].to(device)
     q = torch.randn(layers, n, hq, D, generator=gd, device=device).to(torch.bfloat16)
     kn = torch.randn(layers, n, hkv, D, generator=gd, device=device).to(torch.bfloat16)
     out = torch.empty_like(q)
-    kernel, split, _ = mi.decode_plan(n, hq, hkv, D, torch.bfloat16, BS, 0, device, table.shape[1])
+    kernel, split, _ = mi.decode_plan(n, hq, hkv, D, torch.bfloat16, BS, 0, device,
+                                      table_d.shape[1])
     views = [pool.layer(i) for i in range(pools)]
 
     def run():
         for i in range(layers):
             v = views[i % pools]
             mi.paged_decode_store(q[i], v.keys, v.values, table_d, ctx_d, kn[i], kn[i], slots_d,
-                                  split_k=split, out=out[i], early_kv=True)
+                                  split_k=None, out=out[i], early_kv=True)
 
     run()
     torch.cuda.synchronize(device)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        run()
-    graph.replay()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize(device)
-    ms = e0.elapsed_time(e1) / reps
-    b = layers * (decode_bytes(ctx.tolist(), hq, hkv, D, 2, BS) + store_bytes(n, hkv, D, 2))
-    del graph, pool
+    mi.check_device_status(device)
+    # layer 0 was stored again by later layers sharing its pool: check the last layer
+    last = views[(layers - 1) % pools]
+    bd = dict(b, table=table_d)
+    check = _check_attention(out[layers - 1], q[layers - 1], last.keys, last.values, bd,
+                             [0, n - 1] if n > 1 else [0], "configs[4] run (a)")
+    ms = _graph_ms(device, run, reps, warm=1)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    total = layers * (decode_bytes(full["contexts"], hq, hkv, D, 2, BS)
+                      + store_bytes(len(full["contexts"]), hkv, D, 2))
+    del pool, q, kn, out
+    torch.cuda.empty_cache()
     peaks, src = _peaks()
-    gbs = b / (ms * 1e-3) / 1e9
+    gbs = total / (ms * 1e-3) / 1e9
     return {"workload": "BASELINE configs[4] run (a): 256 seqs, contexts U[4096,32768], 32q/8kv, "
-                        f"D128, 36 layers over {pools} distinct ~19 GB layer pools, bs16",
+                        f"D128, 36 layers, bs16, sequence-sharded over {world} GPU(s) "
+                        "(sharding.assign_sequences by total context)",
+            "scaling": "strong (the 256 sequences are fixed as the GPU count grows)",
+            "per_rank_sequences": n, "distinct_layer_pools_per_rank": pools,
+            "pool_gb_per_rank": round(pools * layer_bytes / 1e9, 1),
             "kernel": kernel, "split_k": split, "ms_per_step": round(ms, 3),
-            "value": round(gbs, 1), "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 4),
-            "peak_source": f"hbm_gbs of {src}", "tok_per_s": round(n * 1000.0 / ms, 1)}
+            "value": round(gbs, 1), "unit": "GB/s", "frac_per_gpu": round(gbs / world / peaks["hbm_gbs"], 4),
+            "peak_source": f"hbm_gbs of {src}", "tok_per_s": round(256 * 1000.0 / ms, 1),
+            "checked": check}
 
 
-def _prefill_batch(workload: str, device, g):
-    """Metadata + per-layer-shaped inputs for BASELINE configs[2] / configs[3]."""
-    import torch
+def _prefill_batch(workload: str, device, g=None):
+    """BASELINE configs[2] ("mixed") / configs[3] ("prefix") on the device
+    (tests/golden/configs.py, the batches the full-size parity tests check)."""
+    from tests.golden import configs
 
-    gen = torch.Generator(device="cpu").manual_seed(3 if workload == "mixed" else 4)
-    if workload == "mixed":
-        # configs[2]: 24 decode sequences ctx U[1,4096] + 8 prefill chunks of 512 on 0..1536 cached
-        dec = torch.randint(1, 4097, (24,), generator=gen)
-        pre_p = torch.randint(0, 1537, (8,), generator=gen)
-        q_lens = [1] * 24 + [512] * 8
-        contexts = dec.tolist() + (pre_p + 512).tolist()
-        need = [(c + BS - 1) // BS for c in contexts]
-        nb = sum(need) + 8
-        perm = torch.randperm(nb, generator=gen).to(torch.int32)
-        table = torch.full((len(contexts), max(need)), -1, dtype=torch.int32)
-        at = 0
-        for r, k in enumerate(need):
-            table[r, :k] = perm[at:at + k]
-            at += k
-    else:
-        # configs[3]: 64 sequences share a 1024-token prefix stored once (64 block ids in
-        # every table); each prefills its own 128-token suffix on top of it
-        n, prefix, suffix = 64, 1024, 128
-        shared = torch.arange(prefix // BS, dtype=torch.int32)
-        q_lens = [suffix] * n
-        contexts = [prefix + suffix] * n
-        per = suffix // BS
-        nb = prefix // BS + n * per + 8
-        table = torch.empty((n, prefix // BS + per), dtype=torch.int32)
-        for r in range(n):
-            table[r, :prefix // BS] = shared
-            table[r, prefix // BS:] = torch.arange(prefix // BS + r * per,
-                                                   prefix // BS + (r + 1) * per)
-    cu_q = torch.tensor([0] + list(torch.cumsum(torch.tensor(q_lens), 0).tolist()), dtype=torch.int32)
-    cu_k = torch.tensor([0] + list(torch.cumsum(torch.tensor(contexts), 0).tolist()), dtype=torch.int32)
-    slots = []
-    for r, (q, c) in enumerate(zip(q_lens, contexts)):
-        for pos in range(c - q, c):
-            slots.append(int(table[r, pos // BS]) * BS + pos % BS)
-    return dict(q_lens=q_lens, contexts=contexts, nb=nb, table=table.to(device),
-                cu_q=cu_q.to(device), cu_k=cu_k.to(device),
-                slots=torch.tensor(slots, dtype=torch.int32, device=device))
+    b = configs.mixed_batch() if workload == "mixed" else configs.shared_prefix_batch()
+    for k in ("table", "cu_q", "cu_k", "slots"):
+        b[k] = b[k].to(device)
+    return b
 
 
 def prefill_kernel_name() -> str:
@@ -381,7 +467,7 @@ def measure_prefill(device, workload: str, layers: int = 28, reps: int = 10):
     import torch
 
     import microinfer_b200 as mi
-    from oracle.paged_oracle import prefill_flops
+    from tests.golden.configs import prefill_flops
 
     g = torch.Generator(device=device).manual_seed(11)
     b = _prefill_batch(workload, device, g)
@@ -404,17 +490,15 @@ def measure_prefill(device, workload: str, layers: int = 28, reps: int = 10):
     run()
     torch.cuda.synchronize(device)
     mi.check_device_status(device)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        run()
-    graph.replay()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize(device)
-    ms_layer = e0.elapsed_time(e1) / reps / layers
+    ctx = b["contexts"]
+    if workload == "mixed":
+        dec = sorted(range(24), key=ctx.__getitem__)
+        rows = [dec[0], dec[-1], 24, 31]
+    else:
+        rows = [0, 63]
+    check = _check_attention(out, q, views[-1].keys, views[-1].values, b, rows,
+                             f"prefill {workload}")
+    ms_layer = _graph_ms(device, run, reps, warm=1) / layers
     flops = prefill_flops(b["q_lens"], b["contexts"], HQ, D)
     kv_bytes = sum(2 * c * HKV * D * 2 for c in b["contexts"])
     if workload == "prefix":  # the shared prefix is stored once
@@ -427,13 +511,268 @@ def measure_prefill(device, workload: str, layers: int = 28, reps: int = 10):
            "kernel": prefill_kernel_name(), "layers": layers,
            "us_per_layer": round(ms_layer * 1e3, 2), "flops_per_layer": flops,
            "tflops": round(tflops, 1), "tensor_frac": round(tflops / peaks["bf16_tflops"], 4),
-           "peak_source": f"bf16_tflops of {src}", "store_tokens": tokens}
+           "peak_source": f"bf16_tflops of {src}", "store_tokens": tokens, "checked": check}
     if workload == "mixed":
         t_min = kv_bytes / (peaks["hbm_gbs"] * 1e9) + flops / (peaks["bf16_tflops"] * 1e12)
         res["combined_bound_frac"] = round(t_min / (ms_layer * 1e-3), 4)
         res["kv_bytes_per_layer"] = kv_bytes
-    del graph, pool
+    del pool
     return res
+
+
+def measure_shared_prefix_step(device, layers: int = LAYERS, decode_steps: int = 16, reps: int = 3):
+    """BASELINE configs[3] as a whole: copy-on-write of a shared partial page,
+    the suffix prefill over the shared prefix, 16 decode steps, and the
+    block-table gather, each timed on its own (28 layers, one CUDA graph).
+
+    The reference never shares a partial page, so to exercise copy-on-write
+    the shared prefix here is 1016 tokens: pages 0..62 full and page 63 holding
+    8 tokens, shared by all 64 sequences.  Each sequence's 128-token suffix
+    starts by appending into page 63, so page 63 is first copied to a private
+    page per sequence (64 (src, dst) pairs x 28 layers x K and V, one launch);
+    the suffix and the 16 decoded tokens then go to the sequence's own pages.
+    Decode is reported as logical GB/s (every sequence's context) and as
+    unique-byte GB/s (the 63 shared pages counted once): the shared prefix
+    stays in L2 across sequences, so logical GB/s can exceed the HBM peak.
+    The gather is the reference's gather-plus-varlen input at the prefill
+    (`_gather_paged_kv`, every sequence's 1144 rows).
+    """
+    import torch
+
+    import microinfer_b200 as mi
+    from tests.golden import configs
+    from tests.golden.configs import (cow_bytes, decode_bytes, gather_bytes, prefill_flops,
+                                      store_bytes)
+
+    n, prefix, suffix = 64, 1016, 128
+    shared_pages = (prefix + BS - 1) // BS          # 64, the last one partial
+    ctx0 = prefix + suffix                           # 1144 after the prefill
+    ctx_end = ctx0 + decode_steps                    # 1160 after the decode steps
+    own = (ctx_end + BS - 1) // BS - (shared_pages - 1)  # private pages per sequence (incl. copy)
+    nb = shared_pages + n * own + 8
+    width = (ctx_end + BS - 1) // BS
+    table = torch.empty(n, width, dtype=torch.int32)
+    pairs = torch.empty(n, 2, dtype=torch.int32)
+    for r in range(n):
+        base = shared_pages + r * own
+        table[r, :shared_pages - 1] = torch.arange(shared_pages - 1)
+        table[r, shared_pages - 1:] = torch.arange(base, base + own)
+        pairs[r] = torch.tensor([shared_pages - 1, base])
+    pre = configs._finish([suffix] * n, [ctx0] * n, table, nb)
+    pool = mi.KVCache(layers, nb, BS, HKV, D, dtype=torch.bfloat16, device=device)
+    g = torch.Generator(device=device).manual_seed(31)
+    pool.keys.normal_(generator=g).mul_(0.5)
+    pool.values.normal_(generator=g).mul_(0.5)
+    views = [pool.layer(i) for i in range(layers)]
+    table_d, pairs_d = table.to(device), pairs.to(device)
+    cu_q, cu_k, slots = pre["cu_q"].to(device), pre["cu_k"].to(device), pre["slots"].to(device)
+    tokens = n * suffix
+    q = torch.randn(tokens, HQ, D, generator=g, device=device).to(torch.bfloat16)
+    kn = torch.randn(tokens, HKV, D, generator=g, device=device).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    qd = torch.randn(decode_steps, n, HQ, D, generator=g, device=device).to(torch.bfloat16)
+    knd = torch.randn(decode_steps, n, HKV, D, generator=g, device=device).to(torch.bfloat16)
+    outd = torch.empty_like(qd)
+    dctx = torch.stack([torch.full((n,), ctx0 + k + 1, dtype=torch.int32)
+                        for k in range(decode_steps)]).to(device)
+    pos = torch.arange(ctx0, ctx_end)
+    dslots = (table[:, pos // BS].long() * BS + (pos % BS)[None, :]).to(torch.int32)
+    dslots = dslots.t().contiguous().to(device)  # [step, seq]
+    _, split, _ = mi.decode_plan(n, HQ, HKV, D, torch.bfloat16, BS, 0, device, width)
+    gk = torch.empty(n * ctx0, HKV, D, dtype=torch.bfloat16, device=device)
+    gv = torch.empty_like(gk)
+
+    def cow():
+        pool.copy_blocks(pairs_d, check=False)
+
+    def prefill():
+        for v in views:
+            v.write_slots(slots, kn, kn)
+            mi.paged_prefill(q, v.keys, v.values, cu_q, cu_k, table_d, max_seqlen_q=suffix,
+                             out=out)
+
+    def decode():
+        for k in range(decode_steps):
+            for v in views:
+                mi.paged_decode_store(qd[k], v.keys, v.values, table_d, dctx[k], knd[k], knd[k],
+                                      dslots[k], split_k=None, out=outd[k], early_kv=True)
+
+    def gather():
+        for v in views:
+            mi.gather_paged_kv(v.keys, v.values, table_d, [ctx0] * n, BS, cu_seqlens_k=cu_k,
+                               out=(gk, gv))
+
+    # --- run each phase once in order and check it before any timing -------------
+    src_k = pool.keys[:, shared_pages - 1].clone()
+    cow()
+    torch.cuda.synchronize(device)
+    for r in (0, n - 1):
+        if not (torch.equal(pool.keys[:, int(pairs[r, 1])], src_k)
+                and torch.equal(pool.values[:, int(pairs[r, 1])], pool.values[:, shared_pages - 1])):
+            raise RuntimeError("shared-prefix step: copy-on-write page differs from its source")
+    del src_k
+    prefill()
+    torch.cuda.synchronize(device)
+    bp = dict(pre, table=table_d)
+    check_p = _check_attention(out, q, views[-1].keys, views[-1].values, bp, [0, n - 1],
+                               "shared-prefix suffix prefill")
+    decode()
+    torch.cuda.synchronize(device)
+    bd = {"cu_q": torch.arange(n + 1, dtype=torch.int32), "table": table_d,
+          "contexts": [ctx_end] * n}
+    check_d = _check_attention(outd[-1], qd[-1], views[-1].keys, views[-1].values, bd, [0, n - 1],
+                               "shared-prefix decode (last step)")
+    gather()
+    torch.cuda.synchronize(device)
+    lk = views[-1].keys
+    for r in (0, n - 1):
+        rows = lk[table_d[r].long()].reshape(-1, HKV, D)[:ctx0]
+        if not torch.equal(gk[r * ctx0:(r + 1) * ctx0], rows):
+            raise RuntimeError("shared-prefix step: gathered rows differ from the pool")
+    mi.check_device_status(device)
+    ms_cow = _graph_ms(device, cow, reps * 10)
+    ms_pre = _graph_ms(device, prefill, reps)
+    ms_dec = _graph_ms(device, decode, reps)
+    ms_gat = _graph_ms(device, gather, reps)
+    mi.check_device_status(device)
+    peaks, src = _peaks()
+    hbm, tf = peaks["hbm_gbs"], peaks["bf16_tflops"]
+    b_cow = cow_bytes(n, layers, BS, HKV, D, 2)
+    f_pre = prefill_flops([suffix] * n, [ctx0] * n, HQ, D)
+    st_pre = store_bytes(tokens, HKV, D, 2)
+    logical = sum(decode_bytes([ctx0 + k + 1] * n, HQ, HKV, D, 2, BS) + store_bytes(n, HKV, D, 2)
+                  for k in range(decode_steps))
+    shared_rows = (shared_pages - 1) * BS
+    unique = sum(2 * (shared_rows + n * (ctx0 + k + 1 - shared_rows)) * HKV * D * 2
+                 + 2 * n * HQ * D * 2 + store_bytes(n, HKV, D, 2)
+                 for k in range(decode_steps))
+    b_gat = gather_bytes([ctx0] * n, HKV, D, 2)
+    del pool, gk, gv
+    torch.cuda.empty_cache()
+    return {
+        "workload": "BASELINE configs[3] whole: 64 seqs on a shared 1016-token prefix (pages 0-62 "
+                    "full, page 63 shared with 8 tokens), CoW of page 63 per sequence, 128-token "
+                    "suffix prefill, 16 decode steps, gather of the 1144-row contexts; 28 layers",
+        "cow": {"kernel": "cow_kernel", "pairs": n, "layers": layers,
+                "us": round(ms_cow * 1e3, 2), "bytes": b_cow,
+                "gbs": round(b_cow / (ms_cow * 1e-3) / 1e9, 1),
+                "hbm_frac": round(b_cow / (ms_cow * 1e-3) / 1e9 / hbm, 4)},
+        "prefill": {"kernel": prefill_kernel_name(), "us_per_layer": round(ms_pre / layers * 1e3, 2),
+                    "tflops": round(f_pre / (ms_pre / layers * 1e-3) / 1e12, 1),
+                    "tensor_frac": round(f_pre / (ms_pre / layers * 1e-3) / 1e12 / tf, 4),
+                    "includes": "store of the 8192 suffix tokens per layer",
+                    "store_bytes_per_layer": st_pre, "checked": check_p},
+        "decode": {"kernel": "paged_decode_mma_kernel (store fused)", "split_k": split,
+                   "us_per_step": round(ms_dec / decode_steps * 1e3, 2),
+                   "us_per_layer": round(ms_dec / decode_steps / layers * 1e3, 3),
+                   "logical_gbs": round(layers * logical / (ms_dec * 1e-3) / 1e9, 1),
+                   "unique_gbs": round(layers * unique / (ms_dec * 1e-3) / 1e9, 1),
+                   "unique_hbm_frac": round(layers * unique / (ms_dec * 1e-3) / 1e9 / hbm, 4),
+                   "checked": check_d},
+        "gather": {"kernel": "gather_kernel", "us_per_layer": round(ms_gat / layers * 1e3, 2),
+                   "bytes_per_layer": b_gat,
+                   "gbs": round(b_gat / (ms_gat / layers * 1e-3) / 1e9, 1),
+                   "hbm_frac": round(b_gat / (ms_gat / layers * 1e-3) / 1e9 / hbm, 4)},
+        "peak_source": f"hbm_gbs / bf16_tflops of {src}",
+    }
+
+
+def measure_store(device, layers: int = LAYERS, reps: int = 20):
+    """Standalone store_kvcache (`store_kv_vec16_kernel`) at the prefill token
+    counts of configs[2] (4120 tokens) and configs[3] (8192), 28 distinct layer
+    pools per step; the written slots are checked bit for bit first."""
+    import torch
+
+    import microinfer_b200 as mi
+    from tests.golden.configs import store_bytes
+
+    peaks, src = _peaks()
+    res = {}
+    for label, b in (("configs[2] 4120 tokens", _prefill_batch("mixed", device)),
+                     ("configs[3] 8192 tokens", _prefill_batch("prefix", device))):
+        pool = mi.KVCache(layers, b["nb"], BS, HKV, D, dtype=torch.bfloat16, device=device)
+        g = torch.Generator(device=device).manual_seed(41)
+        t = b["tokens"]
+        kn = torch.randn(layers, t, HKV, D, generator=g, device=device).to(torch.bfloat16)
+        vn = torch.randn(layers, t, HKV, D, generator=g, device=device).to(torch.bfloat16)
+        views = [pool.layer(i) for i in range(layers)]
+
+        def run():
+            for i, v in enumerate(views):
+                v.write_slots(b["slots"], kn[i], vn[i])
+
+        run()
+        torch.cuda.synchronize(device)
+        sl = b["slots"].long()
+        for i in (0, layers - 1):
+            if not (torch.equal(views[i].keys.view(-1, HKV, D)[sl], kn[i])
+                    and torch.equal(views[i].values.view(-1, HKV, D)[sl], vn[i])):
+                raise RuntimeError("store: written rows differ from the inputs")
+        ms = _graph_ms(device, run, reps) / layers
+        nbytes = store_bytes(t, HKV, D, 2)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        res[label] = {"us_per_launch": round(ms * 1e3, 2), "bytes_per_launch": nbytes,
+                      "gbs": round(gbs, 1), "hbm_frac": round(gbs / peaks["hbm_gbs"], 4)}
+        del pool, kn, vn
+    return {"kernel": "store_kv_vec16_kernel", "checked": "written rows bit-exact",
+            "peak_source": f"hbm_gbs of {src}", "rows": res}
+
+
+def measure_varlen(device, layers: int = LAYERS, reps: int = 10):
+    """Prefix-free (direct) prefill through `varlen_prefill` on a configs[2]-sized
+    batch: 8 x 512 + 24 x U[1, 64] tokens, contiguous K/V, a distinct K/V pair
+    per layer (~0.5 GB over 28 layers, more than L2)."""
+    import torch
+
+    import microinfer_b200 as mi
+    from tests.golden.configs import prefill_flops
+
+    gen = torch.Generator().manual_seed(16)
+    lens = [512] * 8 + torch.randint(1, 65, (24,), generator=gen).tolist()
+    total = sum(lens)
+    g = torch.Generator(device=device).manual_seed(16)
+    q = torch.randn(total, HQ, D, generator=g, device=device).to(torch.bfloat16)
+    k = torch.randn(layers, total, HKV, D, generator=g, device=device).to(torch.bfloat16)
+    v = torch.randn(layers, total, HKV, D, generator=g, device=device).to(torch.bfloat16)
+    cu = torch.zeros(len(lens) + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(torch.tensor(lens), 0)
+    cu_d = cu.to(device)
+    out = torch.empty_like(q)
+
+    def run():
+        for i in range(layers):
+            mi.varlen_prefill(q, k[i], v[i], cu_d, cu_d, max_seqlen_q=512, out=out)
+
+    run()
+    torch.cuda.synchronize(device)
+    mi.check_device_status(device)
+    # the last layer, requests 0 (512 tokens) and 31, against dense causal attention
+    rows, worst = (0, len(lens) - 1), 0.0
+    for r in rows:
+        a, e = int(cu[r]), int(cu[r + 1])
+        n = e - a
+        kk = k[-1, a:e].float().repeat_interleave(HQ // HKV, 1).transpose(0, 1)
+        vv = v[-1, a:e].float().repeat_interleave(HQ // HKV, 1).transpose(0, 1)
+        sc = q[a:e].float().transpose(0, 1) @ kk.transpose(1, 2) / math.sqrt(D)
+        sc = sc.masked_fill(torch.triu(torch.ones(n, n, dtype=torch.bool, device=device), 1),
+                            float("-inf"))
+        ref = (sc.softmax(-1) @ vv).transpose(0, 1)
+        got = out[a:e].float()
+        if not torch.allclose(got, ref, atol=ATOL, rtol=RTOL):
+            raise RuntimeError(f"varlen prefill: request {r} differs from dense attention")
+        worst = max(worst, (got - ref).abs().max().item())
+    ms = _graph_ms(device, run, reps) / layers
+    flops = prefill_flops(lens, lens, HQ, D)
+    peaks, src = _peaks()
+    tfl = flops / (ms * 1e-3) / 1e12
+    del k, v
+    return {"workload": "direct prefill, 8 x 512 + 24 x U[1,64] tokens, 16q/8kv, D128, bf16",
+            "kernel": "prefill_tc2_kernel (dense mode)", "us_per_layer": round(ms * 1e3, 2),
+            "flops_per_layer": flops, "tflops": round(tfl, 1),
+            "tensor_frac": round(tfl / peaks["bf16_tflops"], 4),
+            "peak_source": f"bf16_tflops of {src}",
+            "checked": {"requests_checked": len(rows), "max_abs_err": round(worst, 5),
+                        "against": "fp32 dense causal attention, 2e-2 abs / 1e-2 rel"}}
 
 
 def _prologue_inputs(device, layers: int, tokens: int, g):
@@ -652,9 +991,12 @@ def run_reference(args):
         return
     steps, warmup = args.steps, args.warmup
     budget = max(1.0, min(20.0, 150.0 / max(1, steps + warmup)))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    # The reference's own CPU path when its install is here, else the numpy port.
+    run = reference_cpu_baseline if reference_cpu_baseline(seconds=0.0) else cpu_baseline
     for _ in range(warmup):
-        cpu_baseline(seconds=budget / 4)
-    vals = [cpu_baseline(seconds=budget) for _ in range(max(1, steps))]
+        run(seconds=budget / 4)
+    vals = [run(seconds=budget) for _ in range(max(1, steps))]
     v = statistics.median([x["value"] for x in vals])
     base = vals[0]
     base["value"] = v
@@ -663,13 +1005,14 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": steps, "warmup": warmup,
         "ms_per_step": statistics.median([x["ms_per_28_layer_step"] for x in vals]),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded numpy, BASELINE configs[1] shapes)",
-        "config": {"workload": WORKLOAD, "global_batch": NSEQ, "context": [CTX_LO, CTX_HI],
-                   "layers": LAYERS, "block_size": BS, "heads": [HQ, HKV], "head_dim": D,
-                   "l2": "per-step working set > L2"},
+        "data": "synthetic (seeded, BASELINE configs[1] shapes)",
+        "config": bench_config(world),
         "cpu_baseline": base,
         "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if world > 1:
+        line["note"] = ("one host: rank 0 alone times one GPU's shard (8 sequences) of the "
+                        "workload on every host core; the other ranks exit without work")
     print(json.dumps(line), flush=True)
 
 
@@ -695,7 +1038,7 @@ def run_reference_gpu(args):
     from microinfer.layer.triton_paged_attention import triton_paged_decode, triton_paged_prefill
     from microinfer.worker.triton_kv_store import store_kv
 
-    from oracle.paged_oracle import decode_bytes, prefill_flops, store_bytes
+    from tests.golden.configs import decode_bytes, prefill_flops, store_bytes
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -951,7 +1294,7 @@ def run_ours(args):
             # Layer i+1's launch only follows layer i's decode, which writes neither
             # layer i+1's pool nor the tables: its pages may load early (PDL).
             mi.paged_decode_store(q[i], view.keys, view.values, table_d, ctx_d, kn[i], vn[i],
-                                  slots_d, split_k=split, out=out[i], early_kv=True)
+                                  slots_d, split_k=None, out=out[i], early_kv=True)
 
     def sample(slot=0):
         # stand-in sampler: one int32 token id per sequence from the last layer
@@ -972,41 +1315,48 @@ def run_ours(args):
             decode_only()
     torch.cuda.current_stream(device).wait_stream(stream)
     torch.cuda.synchronize(device)
+    cur = torch.cuda.current_stream(device)
+    gathered = torch.empty(2, world * NSEQ, dtype=torch.int32, device=device)
+    ag_stream = torch.cuda.Stream(device)
+    if world > 1:  # communicators exist before any capture
+        dist.all_gather_into_tensor(gathered[0], tokens_buf[0])
+        torch.cuda.synchronize(device)
+    # One CUDA graph per step, double-buffered on the token slot: graph `slot` runs
+    # the 28 layers and the sampler into tokens_buf[slot] and, on a side branch that
+    # overlaps those layers, the NCCL all_gather of the previous step's token ids
+    # (tokens_buf[1 - slot], for the scheduler; the attention never waits on it).  The
+    # host issues one graph launch per step, so the ranks' steps are paced by the GPU,
+    # not by Python and NCCL issue.  The last step's gather runs after the loop, inside
+    # the timed region.
     graphs = []
     for slot in range(2):
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr):
+            cs = torch.cuda.current_stream(device)
+            if world > 1:
+                ag_stream.wait_stream(cs)
+                with torch.cuda.stream(ag_stream):
+                    dist.all_gather_into_tensor(gathered[1 - slot], tokens_buf[1 - slot])
             layer_loop(slot)
+            if world > 1:
+                cs.wait_stream(ag_stream)
         graphs.append(gr)
-    graph = graphs[0]
     dgraph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(dgraph):
         decode_only()
-    cur = torch.cuda.current_stream(device)
-    gathered = torch.empty(2, world * NSEQ, dtype=torch.int32, device=device)
-    ag_stream = torch.cuda.Stream(device)
-    ag_ready = [torch.cuda.Event() for _ in range(2)]
-    ag_done = [torch.cuda.Event() for _ in range(2)]
 
     def step(k):
-        # One decode step: 28 layers + sampler into tokens_buf[k % 2], then the
-        # all_gather of those token ids (for the scheduler, off the attention path)
-        # on its own stream, overlapping the next step's layers; step k+2 reuses
-        # the buffer only after that gather is done.
-        slot = k & 1
-        if world > 1:
-            cur.wait_event(ag_done[slot])
-        graphs[slot].replay()
-        if world > 1:
-            ag_ready[slot].record(cur)
-            ag_stream.wait_event(ag_ready[slot])
-            with torch.cuda.stream(ag_stream):
-                dist.all_gather_into_tensor(gathered[slot], tokens_buf[slot])
-            ag_done[slot].record(ag_stream)
+        graphs[k & 1].replay()
 
-    for k in range(max(3, args.warmup)):
+    def last_gather(k_last):
+        if world > 1:
+            slot = k_last & 1
+            dist.all_gather_into_tensor(gathered[slot], tokens_buf[slot])
+
+    warm = max(3, args.warmup)
+    for k in range(warm):
         step(k)
-    cur.wait_stream(ag_stream)
+    last_gather(warm - 1)
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
@@ -1022,23 +1372,32 @@ def run_ours(args):
             starts[k].record(cur)
             step(k)
             ends[k].record(cur)
-        cur.wait_stream(ag_stream)  # the last step's gather ends inside the timed region
+        last_gather(args.steps - 1)  # the last step's gather ends inside the timed region
         t_all1.record(cur)
         torch.cuda.synchronize(device)
-        # keep sampling clocks over ~1 s of the same step (not timed)
+        # keep sampling clocks over ~1 s of the decode layers (not timed; no collective,
+        # so the ranks need not replay it equally often)
         if len(clocks.samples) < 20:
             t_end = time.time() + 1.0
             while time.time() < t_end:
                 for _ in range(50):
-                    graph.replay()
+                    dgraph.replay()
                 torch.cuda.synchronize(device)
     total_ms = t_all0.elapsed_time(t_all1)
     per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    # device idle time between consecutive steps (host issue gaps)
+    gaps = [ends[k].elapsed_time(starts[k + 1]) for k in range(args.steps - 1)]
     ms_step = total_ms / args.steps
+    gap_stats = [statistics.median(gaps) * 1e3 if gaps else 0.0, max(gaps) * 1e3 if gaps else 0.0]
     if world > 1:
-        t = torch.tensor([ms_step], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms_step = float(t.item())
+        t = torch.tensor([ms_step, gap_stats[0], gap_stats[1]], device=device)
+        every = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(every, t)
+        ms_step = max(float(x[0]) for x in every)
+        gap_stats = [max(float(x[1]) for x in every), max(float(x[2]) for x in every)]
+        rank_ms = [round(float(x[0]), 5) for x in every]
+    else:
+        rank_ms = [round(ms_step, 5)]
 
     dec_b, st_b = algorithmic_bytes(ctx.tolist())
     step_bytes = LAYERS * (dec_b + st_b)
@@ -1057,6 +1416,30 @@ def run_ours(args):
     decode_launch_ms = e0.elapsed_time(e1) / (reps * LAYERS)
     peaks, peak_src = _peaks()
     achieved = (dec_b + st_b) / (decode_launch_ms * 1e-3) / 1e9
+
+    # --- the same launches isolated, as the model runs them: each layer's decode follows
+    # a GEMM (the 1024 x 4096 x 3072 bf16 product standing in for a layer's projections)
+    # that occupies every SM, so no page load starts early.  Per-layer decode cost =
+    # (graph of 28 x [GEMM, decode]) - (graph of 28 x [GEMM]), both by CUDA events.
+    ga = torch.randn(1024, 4096, device=device, dtype=torch.bfloat16)
+    gb = torch.randn(4096, 3072, device=device, dtype=torch.bfloat16)
+    gc = torch.empty(1024, 3072, device=device, dtype=torch.bfloat16)
+
+    def gemm_layers(with_decode):
+        for i in range(LAYERS):
+            torch.mm(ga, gb, out=gc)
+            if with_decode:
+                view = views[i]
+                mi.paged_decode_store(q[i], view.keys, view.values, table_d, ctx_d, kn[i], vn[i],
+                                      slots_d, split_k=None, out=out[i], early_kv=True)
+
+    gemm_layers(True)
+    torch.cuda.synchronize(device)
+    iso_both = _graph_ms(device, lambda: gemm_layers(True), 20, warm=3)
+    iso_gemm = _graph_ms(device, lambda: gemm_layers(False), 20, warm=3)
+    iso_avg_us = (iso_both - iso_gemm) / LAYERS * 1e3
+    iso_gbs = (dec_b + st_b) / (iso_avg_us * 1e-6) / 1e9
+    del ga, gb, gc
 
     # --- e2e: host buffers through the public API ----------------------------
     # Every step copies its inputs in from pinned host memory and its results (the
@@ -1159,16 +1542,18 @@ def run_ours(args):
             "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded torch, BASELINE configs[1] shapes), random-init pool",
-            "config": {"workload": WORKLOAD, "global_batch": NSEQ * world, "per_gpu_batch": NSEQ,
-                       "context": [CTX_LO, CTX_HI], "layers": LAYERS, "block_size": BS,
-                       "num_blocks_per_layer": NB, "heads": [HQ, HKV], "head_dim": D,
-                       "split_k": split, "decode_kernel": decode_kernel,
-                       "parallelism": f"sequence-sharded x{world}",
-                       "l2": "inputs larger than L2: 28 distinct layer pools, "
-                             f"{step_bytes / 1e6:.0f} MB touched per step",
-                       "graph": "28-layer store+decode CUDA graph replay"},
+            "config": bench_config(world),
+            "plan": {"split_k": split, "decode_kernel": decode_kernel,
+                     "bytes_per_step_per_gpu": step_bytes,
+                     "graph": "one CUDA graph per step: 28 store+decode launches, the sampler "
+                              "and (N > 1) the previous step's token all_gather on a side "
+                              "branch"},
             "tok_per_s": round(world * NSEQ / (ms_step * 1e-3), 1),
             "median_step_ms": round(statistics.median(per_step), 5),
+            "rank_ms_per_step": rank_ms,
+            "step_gap_us": {"median": round(gap_stats[0], 2), "max": round(gap_stats[1], 2),
+                            "what": "device idle time between one step's end and the next "
+                                    "step's start, max over ranks"},
             "roofline": {"bound": "hbm",
                          "kernel": DECODE_KERNEL_NAMES.get(decode_kernel, decode_kernel)
                                    + " (store fused, split merge)",
@@ -1181,7 +1566,16 @@ def run_ours(args):
                          "traffic": _profiled_traffic(DECODE_PROFILES.get(decode_kernel, "")),
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, "
                                            "profiles/ summary of the same kernel and shapes",
-                         "step_frac": round(value / world / peaks["hbm_gbs"], 4)},
+                         "step_frac": round(value / world / peaks["hbm_gbs"], 4),
+                         "timing": "average launch in a 28-layer decode-only graph replay "
+                                   "(back to back: a layer's page loads may start under the "
+                                   "previous layer's tail)",
+                         "isolated": {"avg_launch_us": round(iso_avg_us, 3),
+                                      "achieved": round(iso_gbs, 1),
+                                      "frac": round(iso_gbs / peaks["hbm_gbs"], 4),
+                                      "what": "per-layer decode cost behind a GEMM that fills "
+                                              "every SM (28 x [GEMM, decode] graph minus 28 x "
+                                              "[GEMM] graph); no early start"}},
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
                     "path": ("pinned host inputs -> microinfer_b200 API (C ABI) -> host outputs; "
@@ -1201,17 +1595,29 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
         }
+    torch.cuda.synchronize(device)
+    del graphs, dgraph  # graphs holding NCCL calls go before the process group
+    del pool, pk_d, out
+    torch.cuda.empty_cache()
+    # configs[4] run (a), sequence-sharded over every rank (each rank times its shard)
+    extra = {"long_context_batch256": measure_long_batch(device, world, rank)}
+    if rank == 0:
         if world == 1:
-            line["extra"] = {"long_context_b1": measure_long_b1(device),
-                             "long_context_batch256": measure_long_batch(device),
-                             "prefill_mixed": measure_prefill(device, "mixed"),
-                             "prefill_shared_prefix": measure_prefill(device, "prefix"),
-                             "attention_prologue": measure_prologue(device),
-                             "runner_metadata": measure_runner_metadata(device)}
+            extra.update({"long_context_b1": measure_long_b1(device),
+                          "prefill_mixed": measure_prefill(device, "mixed"),
+                          "prefill_shared_prefix": measure_prefill(device, "prefix"),
+                          "shared_prefix_step": measure_shared_prefix_step(device),
+                          "store_kv": measure_store(device),
+                          "direct_prefill": measure_varlen(device),
+                          "attention_prologue": measure_prologue(device),
+                          "runner_metadata": measure_runner_metadata(device)})
+        line["extra"] = extra
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline()
+            ref_cpu = reference_cpu_baseline()
+            line["cpu_baseline"] = ref_cpu if ref_cpu is not None else cpu_baseline()
+            if ref_cpu is not None:
+                line["cpu_baseline_port"] = cpu_baseline(seconds=6.0)
         print(json.dumps(line), flush=True)
-    del graph, graphs, dgraph
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1248,10 +1654,10 @@ def run_profile(args):
             for i in range(layers):
                 view = pool.layer(i)
                 mi.paged_decode_store(q[i], view.keys, view.values, table, ctx, kn[i], kn[i],
-                                      slots, split_k=split, early_kv=True)
+                                      slots, split_k=args.split_k or None, early_kv=True)
         torch.cuda.synchronize(device)
         mi.check_device_status(device)
-        from oracle.paged_oracle import decode_bytes
+        from tests.golden.configs import decode_bytes
 
         print(json.dumps({"profile": "long", "kernel": kernel, "split_k": split,
                           "decode_bytes_per_launch": decode_bytes([ctx_len], hq, hkv, D, 2, BS)}))
@@ -1316,7 +1722,7 @@ def run_profile(args):
                                  max_seqlen_q=max(b["q_lens"]))
         torch.cuda.synchronize(device)
         mi.check_device_status(device)
-        from oracle.paged_oracle import prefill_flops
+        from tests.golden.configs import prefill_flops
 
         print(json.dumps({"profile": args.profile, "layers": layers, "iterations": args.steps,
                           "flops_per_launch": prefill_flops(b["q_lens"], b["contexts"], HQ, D)}))
@@ -1336,7 +1742,7 @@ def run_profile(args):
         for i in range(layers):
             view = pool.layer(i)
             mi.paged_decode_store(q[i], view.keys, view.values, table_d, ctx_d, kn[i], kn[i],
-                                  slots_d, split_k=split)
+                                  slots_d, split_k=args.split_k or None)
     torch.cuda.synchronize(device)
     mi.check_device_status(device)
     dec_b, _ = algorithmic_bytes(ctx.tolist())

@@ -27,7 +27,7 @@ cudaError_t launch_qk_prologue(const QkPrologueParams &p, int dtype, int D, cuda
 cudaError_t launch_decode_meta(const RunnerMetaParams &p, cudaStream_t stream);
 cudaError_t launch_prefill_meta(const RunnerMetaParams &p, cudaStream_t stream);
 cudaError_t launch_decode_mma(const DecodeParams &d, int dtype, int D, int G, int64_t num_seqs,
-                              int nsplit, cudaStream_t stream);
+                              int nsplit, bool pair, cudaStream_t stream);
 cudaError_t launch_decode_fast(const DecodeParams &p, int dtype, int D, int G, int64_t num_seqs,
                                int nsplit, bool wide, cudaStream_t stream);
 bool decode_wide_supported(int dtype, int D, int G);
@@ -410,8 +410,9 @@ bool decode_uses_workspace(int nsplit) { return nsplit > 1; }
 // Decode kernels, in order of preference: warp-level tensor-core MMA
 // (mma.sync, bf16/fp16, D 64/128, block size a multiple of 16), SIMT
 // (TMA-staged, CUDA cores, every fast shape), generic (any shape).
-// MICROINFER_B200_DECODE=simt|mma pins one of the fast kernels.
-constexpr int kDecodeGeneric = 1, kDecodeSimt = 2, kDecodeMma = 4;
+// MICROINFER_B200_DECODE=simt|mma pins one of the fast kernels.  Plan code 5
+// is the mma kernel in cluster pairs (decode_pair_for).
+constexpr int kDecodeGeneric = 1, kDecodeSimt = 2, kDecodeMma = 4, kDecodeMmaPair = 5;
 
 int decode_kernel_for(int dtype, int D, int G, int block_size, bool aligned, int64_t max_context) {
   (void)max_context;
@@ -442,6 +443,23 @@ int decode_splits_for(int kernel, int64_t num_seqs, int num_kv_heads, int num_sp
   }
   const int64_t hint = ctx_bound > INT32_MAX ? INT32_MAX : ctx_bound;
   return mi_paged_decode_default_splits(num_seqs, num_kv_heads, static_cast<int32_t>(hint), dev);
+}
+
+// Automatic splits of the mma kernel for small batches: instead of one CTA per
+// (sequence, kv head) on at most half the SMs, a cluster of two CTAs per pair
+// takes every other 16-key chunk and merges through distributed shared memory
+// (no workspace, no global round trips), so each pair streams through two SMs.
+// Taken when the pairs fill at most half the SMs and the automatic split count
+// is at most 2; MICROINFER_B200_DECODE_PAIR=0 turns it off.
+bool decode_pair_for(int kernel, int64_t num_seqs, int num_kv_heads, int num_splits, int dev,
+                     int64_t ctx_bound) {
+  static const bool enabled = [] {
+    const char *v = std::getenv("MICROINFER_B200_DECODE_PAIR");
+    return !(v != nullptr && std::strcmp(v, "0") == 0);
+  }();
+  if (!enabled || num_splits != 0 || kernel != kDecodeMma) return false;
+  if (2 * num_seqs * num_kv_heads > sm_count_of(dev)) return false;
+  return decode_splits_for(kernel, num_seqs, num_kv_heads, 0, dev, ctx_bound) <= 2;
 }
 
 struct NewToken {
@@ -531,8 +549,11 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
     p.status = dev_status;
     return cuda_status(launch_attn_generic(p, dtype, true, st));
   }
-  const int nsplit = decode_splits_for(kernel, num_seqs, num_kv_heads, num_splits, dev,
-                                       block_table_stride * block_size);
+  const bool pair = decode_pair_for(kernel, num_seqs, num_kv_heads, num_splits, dev,
+                                    block_table_stride * block_size);
+  const int nsplit = pair ? 2
+                          : decode_splits_for(kernel, num_seqs, num_kv_heads, num_splits, dev,
+                                              block_table_stride * block_size);
   DecodeParams p = {};
   p.out = out;
   p.query = query;
@@ -553,7 +574,7 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
     p.slot_mapping = nt->slots;
     p.new_token_stride_bytes = nt->stride * e;
   }
-  if (decode_uses_workspace(nsplit)) {
+  if (!pair && decode_uses_workspace(nsplit)) {
     if (num_seqs * num_kv_heads > kSplitCounters)
       return fail(MI_ERR_UNSUPPORTED, "split-K decode takes at most 16384 (sequence, kv head) "
                                       "pairs per launch; use num_splits=1 or smaller batches");
@@ -569,7 +590,7 @@ int decode_impl(void *out, const void *query, const void *key_cache, const void 
     p.early_kv = 1;
   }
   if (kernel == kDecodeMma) {
-    const cudaError_t me = launch_decode_mma(p, dtype, head_dim, G, num_seqs, nsplit, st);
+    const cudaError_t me = launch_decode_mma(p, dtype, head_dim, G, num_seqs, nsplit, pair, st);
     if (me != cudaErrorNotSupported) return cuda_status(me);
   }
   return cuda_status(launch_decode_fast(p, dtype, head_dim, G, num_seqs, nsplit,
@@ -595,7 +616,14 @@ int mi_paged_decode_plan(int64_t num_seqs, int32_t num_q_heads, int32_t num_kv_h
     return fail(MI_ERR_INVALID, "invalid decode shape");
   const int kernel = decode_kernel_for(dtype, head_dim, num_q_heads / num_kv_heads, block_size, true,
                                        block_table_stride * block_size);
-  const int s = decode_splits_for(kernel, num_seqs, num_kv_heads, num_splits, device < 0 ? 0 : device,
+  const int dev = device < 0 ? 0 : device;
+  if (decode_pair_for(kernel, num_seqs, num_kv_heads, num_splits, dev,
+                      block_table_stride * block_size)) {
+    if (splits_out) *splits_out = 2;
+    if (workspace_bytes_out) *workspace_bytes_out = 0;
+    return kDecodeMmaPair;
+  }
+  const int s = decode_splits_for(kernel, num_seqs, num_kv_heads, num_splits, dev,
                                   block_table_stride * block_size);
   if (splits_out) *splits_out = s;
   if (workspace_bytes_out)
@@ -716,7 +744,7 @@ static int prefill_common(void *out, const void *query, const void *kbase, const
     d.status = dev_status;
     d.cu_q = cu_q;
     d.cu_k = cu_k;
-    return cuda_status(launch_decode_mma(d, dtype, head_dim, G, num_seqs, 1, st));
+    return cuda_status(launch_decode_mma(d, dtype, head_dim, G, num_seqs, 1, false, st));
   }
   return cuda_status(launch_attn_generic(p, dtype, paged, st));
 }

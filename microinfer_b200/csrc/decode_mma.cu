@@ -59,7 +59,9 @@ struct MmaCfg {
   static constexpr int kSmemStages = kWarpsM * kStagesM * kStageBytes;
   static constexpr int kSmemPT = kWarpsM * 256;   // per warp: P^T of a chunk, [16 keys][8 queries]
   static constexpr int kSmemBars = kWarpsM * kStagesM * 8;
-  static constexpr int kSmem = kSmemStages + kSmemPT + kSmemBars + 16 + 1024;  // + slack
+  // cluster pair: the second CTA's merged state, (m, l) then acc, for up to 8 heads
+  static constexpr int kSmemX = 8 * (D + 2) * 4;
+  static constexpr int kSmem = kSmemStages + kSmemPT + kSmemBars + 16 + kSmemX + 1024;  // + slack
   static_assert(kWarpsM * 8 * (D + 2) * 4 <= kSmemStages, "merge buffers alias the ring");
 };
 
@@ -142,7 +144,32 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 
 }  // namespace
 
-template <typename T, int D, int G>
+// Cluster barrier halves (every thread of both CTAs of a pair executes each).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Store to the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ void st_cluster_f32(const float *local, uint32_t rank, float v) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_addr(local)), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(remote), "f"(v) : "memory");
+}
+
+// kPair: the two CTAs of a (sequence, kv head) form a cluster of 2 (grid.x = 2,
+// split = rank); each takes every other 16-key chunk, and rank 1 hands its
+// merged state to rank 0 through distributed shared memory instead of the
+// global workspace.  Two cluster barrier phases: the first (arrive at the start,
+// wait before the first remote store) makes sure rank 0 is running; the second
+// (rank 1 arrives after its stores) hands them over and keeps rank 0's shared
+// memory alive until they have landed.  Neither barrier can be left waiting:
+// every other wait in the kernel is bounded and every path reaches both.
+template <typename T, int D, int G, bool kPair>
 __global__ void __launch_bounds__(kWarpsM * 32, 1)
     paged_decode_mma_kernel(const __grid_constant__ DecodeMmaParams P) {
   using C = MmaCfg<D>;
@@ -153,6 +180,9 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
   uint8_t *pt_smem = smem + C::kSmemStages;
   uint64_t *bars = reinterpret_cast<uint64_t *>(pt_smem + C::kSmemPT);
   int *last_flag = reinterpret_cast<int *>(bars + kWarpsM * kStagesM);
+  float *xml = reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(last_flag) + 16);  // [8][2]
+  float *xacc = xml + 16;                                                              // [8][D]
+  if constexpr (kPair) cluster_arrive_relaxed();
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;  // fragment row / column pair
@@ -461,7 +491,13 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+  constexpr int kIter = (G * D + kWarpsM * 32 - 1) / (kWarpsM * 32);
+  float keep_m[kIter], keep_l[kIter], keep_a[kIter];
+  if constexpr (kPair) cluster_wait_acquire();  // phase 1: rank 0 is running
+#pragma unroll
+  for (int k = 0; k < kIter; ++k) {
+    const int i = threadIdx.x + k * kWarpsM * 32;
+    if (i >= G * D) break;
     const int h = i / D, d = i % D;
     float M = -INFINITY;
 #pragma unroll
@@ -475,24 +511,55 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
       A += f * mg_acc[(w * G + h) * D + d];
     }
     const int qh = kvh * G + h;
-    if (nsplit == 1) {
+    if constexpr (kPair) {
+      if (split == 1) {
+        st_cluster_f32(xacc + h * D + d, 0, A);
+        if (d == 0) {
+          st_cluster_f32(xml + h * 2, 0, M);
+          st_cluster_f32(xml + h * 2 + 1, 0, L);
+        }
+      }
+      keep_m[k] = M;
+      keep_l[k] = L;
+      keep_a[k] = A;
+    } else if (nsplit == 1) {
       T *out = static_cast<T *>(p.out) + (qo_row * p.num_q_heads + qh) * D;
       out[d] = Elem<T>::from_float(L > 0.f ? A / L : 0.f);
     } else {
       split_store_state(p, seq, qh, nsplit, split, D, d, M, L, A);
     }
   }
-  if (nsplit > 1) split_arrive_and_merge<T, G, D>(p, seq, kvh, nsplit, last_flag);
+  if constexpr (kPair) {
+    cluster_arrive_release();  // phase 2: rank 1's state is in rank 0's shared memory
+    cluster_wait_acquire();
+    if (split == 0) {
+#pragma unroll
+      for (int k = 0; k < kIter; ++k) {
+        const int i = threadIdx.x + k * kWarpsM * 32;
+        if (i >= G * D) break;
+        const int h = i / D, d = i % D;
+        const float m1 = xml[h * 2], l1 = xml[h * 2 + 1], a1 = xacc[h * D + d];
+        const float M = fmaxf(keep_m[k], m1);
+        const float f0 = keep_m[k] == -INFINITY ? 0.f : fast_exp2(keep_m[k] - M);
+        const float f1 = m1 == -INFINITY ? 0.f : fast_exp2(m1 - M);
+        const float L = f0 * keep_l[k] + f1 * l1, A = f0 * keep_a[k] + f1 * a1;
+        T *out = static_cast<T *>(p.out) + (qo_row * p.num_q_heads + kvh * G + h) * D;
+        out[d] = Elem<T>::from_float(L > 0.f ? A / L : 0.f);
+      }
+    }
+  } else if (nsplit > 1) {
+    split_arrive_and_merge<T, G, D>(p, seq, kvh, nsplit, last_flag);
+  }
   if (waits_for_prefill) pdl_wait();
 }
 
 namespace {
 
-template <typename T, int D, int G>
-cudaError_t launch_mma_tdg(const DecodeMmaParams &P, int64_t num_seqs, int nsplit,
-                           cudaStream_t stream) {
+template <typename T, int D, int G, bool kPair>
+cudaError_t launch_mma_tdgp(const DecodeMmaParams &P, int64_t num_seqs, int nsplit,
+                            cudaStream_t stream) {
   using C = MmaCfg<D>;
-  auto kern = paged_decode_mma_kernel<T, D, G>;
+  auto kern = paged_decode_mma_kernel<T, D, G, kPair>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -501,17 +568,25 @@ cudaError_t launch_mma_tdg(const DecodeMmaParams &P, int64_t num_seqs, int nspli
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  const dim3 grid(nsplit, P.d.num_kv_heads, static_cast<unsigned>(num_seqs));
-  return launch_pdl(kern, grid, dim3(kWarpsM * 32), C::kSmem, stream, P);
+  const dim3 grid(kPair ? 2 : nsplit, P.d.num_kv_heads, static_cast<unsigned>(num_seqs));
+  return launch_pdl(kern, grid, dim3(kWarpsM * 32), C::kSmem, stream, kPair ? 2u : 1u, P);
+}
+
+template <typename T, int D, int G>
+cudaError_t launch_mma_tdg(const DecodeMmaParams &P, int64_t num_seqs, int nsplit, bool pair,
+                           cudaStream_t stream) {
+  return pair ? launch_mma_tdgp<T, D, G, true>(P, num_seqs, 2, stream)
+              : launch_mma_tdgp<T, D, G, false>(P, num_seqs, nsplit, stream);
 }
 
 template <typename T, int D>
-cudaError_t launch_mma_td(const DecodeMmaParams &P, int G, int64_t n, int s, cudaStream_t st) {
+cudaError_t launch_mma_td(const DecodeMmaParams &P, int G, int64_t n, int s, bool pair,
+                          cudaStream_t st) {
   switch (G) {
-    case 1: return launch_mma_tdg<T, D, 1>(P, n, s, st);
-    case 2: return launch_mma_tdg<T, D, 2>(P, n, s, st);
-    case 4: return launch_mma_tdg<T, D, 4>(P, n, s, st);
-    case 8: return launch_mma_tdg<T, D, 8>(P, n, s, st);
+    case 1: return launch_mma_tdg<T, D, 1>(P, n, s, pair, st);
+    case 2: return launch_mma_tdg<T, D, 2>(P, n, s, pair, st);
+    case 4: return launch_mma_tdg<T, D, 4>(P, n, s, pair, st);
+    case 8: return launch_mma_tdg<T, D, 8>(P, n, s, pair, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -527,7 +602,8 @@ bool decode_mma_supported(int dtype, int D, int G, int block_size) {
 }
 
 cudaError_t launch_decode_mma(const DecodeParams &d, int dtype, int D, int G, int64_t num_seqs,
-                              int nsplit, cudaStream_t stream) {
+                              int nsplit, bool pair, cudaStream_t stream) {
+  if (pair && (d.cu_q != nullptr || nsplit != 2)) return cudaErrorInvalidValue;
   const uint64_t rows = static_cast<uint64_t>(d.num_blocks) * d.block_size;
   if (rows == 0 || rows >= (1ull << 31) || num_seqs > 65535 || nsplit > 65535)
     return cudaErrorNotSupported;
@@ -544,10 +620,10 @@ cudaError_t launch_decode_mma(const DecodeParams &d, int dtype, int D, int G, in
                        row_stride, 64, 1, kChunk, CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorNotSupported;
   if (dtype == MI_DTYPE_BFLOAT16)
-    return D == 64 ? launch_mma_td<__nv_bfloat16, 64>(P, G, num_seqs, nsplit, stream)
-                   : launch_mma_td<__nv_bfloat16, 128>(P, G, num_seqs, nsplit, stream);
-  return D == 64 ? launch_mma_td<__half, 64>(P, G, num_seqs, nsplit, stream)
-                 : launch_mma_td<__half, 128>(P, G, num_seqs, nsplit, stream);
+    return D == 64 ? launch_mma_td<__nv_bfloat16, 64>(P, G, num_seqs, nsplit, pair, stream)
+                   : launch_mma_td<__nv_bfloat16, 128>(P, G, num_seqs, nsplit, pair, stream);
+  return D == 64 ? launch_mma_td<__half, 64>(P, G, num_seqs, nsplit, pair, stream)
+                 : launch_mma_td<__half, 128>(P, G, num_seqs, nsplit, pair, stream);
 }
 
 }  // namespace mi

@@ -87,7 +87,7 @@ def select_split_k(num_requests: int, num_kv_heads: int, device=None,
     return _lib.load().mi_paged_decode_default_splits(num_requests, num_kv_heads, max_context, dev)
 
 
-DECODE_KERNELS = {1: "generic", 2: "simt", 4: "mma"}
+DECODE_KERNELS = {1: "generic", 2: "simt", 4: "mma", 5: "mma_pair"}
 
 
 def decode_plan(num_requests: int, num_q_heads: int, num_kv_heads: int, head_dim: int,
@@ -124,9 +124,11 @@ def _decode_prep(query, key_cache, value_cache, block_tables, context_lens, spli
         raise ValueError("split_k must be a positive int (or None for automatic)")
     if not (key_cache.is_contiguous() and value_cache.is_contiguous()):
         raise ValueError("KV caches must be contiguous")
-    _, split_k, ws_bytes = decode_plan(num_requests, num_q_heads, num_kv_heads, head_dim,
-                                       query.dtype, block_size, split_k, device,
-                                       block_tables.shape[1])
+    # The library plans again from the same shapes; only the workspace size is needed
+    # here, and split_k goes through as given (0 = automatic, which may pick the
+    # cluster-pair kernel that needs no workspace).
+    _, _, ws_bytes = decode_plan(num_requests, num_q_heads, num_kv_heads, head_dim,
+                                 query.dtype, block_size, split_k, device, block_tables.shape[1])
     workspace = _split_workspace(device, ws_bytes) if ws_bytes else None
     return dict(
         query=query.contiguous(), block_tables=_idx(block_tables), context_lens=_idx(context_lens),
@@ -296,12 +298,13 @@ def varlen_prefill(query, keys, values, cu_seqlens_q, cu_seqlens_k, *, max_seqle
 
 
 def gather_paged_kv(key_cache, value_cache, block_tables, contexts, block_size,
-                    *, cu_seqlens_k: torch.Tensor | None = None):
+                    *, cu_seqlens_k: torch.Tensor | None = None, out=None):
     """Valid rows of each request in logical order, concatenated request-major.
 
     ``contexts`` is a host sequence of context lengths (the reference's
     argument); pass ``cu_seqlens_k`` (device, cumulative) to skip the host
-    prefix sum and its copy.
+    prefix sum and its copy, and ``out=(keys, values)`` (contiguous
+    ``[sum(contexts), Hkv, D]``) to write into existing tensors.
     """
     if key_cache.ndim != 4 or value_cache.shape != key_cache.shape:
         raise ValueError("caches must be matching [blocks, block_size, Hkv, D] tensors")
@@ -315,8 +318,18 @@ def gather_paged_kv(key_cache, value_cache, block_tables, contexts, block_size,
         raise ValueError("one context per block-table row")
     total = sum(contexts)
     _, _, num_kv_heads, head_dim = key_cache.shape
-    keys = torch.empty((total, num_kv_heads, head_dim), dtype=key_cache.dtype, device=device)
-    values = torch.empty_like(keys)
+    if out is None:
+        keys = torch.empty((total, num_kv_heads, head_dim), dtype=key_cache.dtype, device=device)
+        values = torch.empty_like(keys)
+    else:
+        keys, values = out
+        want = (total, num_kv_heads, head_dim)
+        if (tuple(keys.shape) != want or tuple(values.shape) != want
+                or keys.dtype != key_cache.dtype or values.dtype != key_cache.dtype
+                or not (keys.is_contiguous() and values.is_contiguous())):
+            raise ValueError("out must be two contiguous [sum(contexts), Hkv, D] tensors of "
+                             "the cache dtype")
+        _lib.require_cuda(keys, values)
     if total == 0:
         return keys, values
     if cu_seqlens_k is None:

@@ -122,3 +122,37 @@ def torch_paged_attention(query, key_cache, value_cache, block_tables, contexts,
         o = torch.einsum("hgqk,khd->qhgd", torch.softmax(score, dim=-1), v)
         out[s:e] = o.reshape(e - s, hq, d).to(query.dtype)
     return out
+
+
+# ---------------------------------------------------------------------------
+# Algorithmic work (the roofline numerators), e = element bytes
+# ---------------------------------------------------------------------------
+def decode_bytes(contexts, hq, hkv, d, e, bs):
+    """K/V read once per kv head + Q read + O written + table entries + lengths."""
+    kv = sum(2 * int(c) * hkv * d * e for c in contexts)
+    return kv + 2 * len(contexts) * hq * d * e + 4 * sum((int(c) + bs - 1) // bs
+                                                         for c in contexts) + 4 * len(contexts)
+
+
+def store_bytes(tokens, hkv, d, e):
+    """K/V rows read and written + one int32 slot per token."""
+    return 4 * tokens * hkv * d * e + 4 * tokens
+
+
+def prefill_flops(q_lens, contexts, hq, d):
+    """Exact causal (query, key) pairs x 2 GEMMs x 2 flops."""
+    pairs = 0
+    for q, c in zip(q_lens, contexts):
+        p = int(c) - int(q)
+        pairs += int(q) * p + int(q) * (int(q) + 1) // 2
+    return 4 * hq * d * pairs
+
+
+def gather_bytes(contexts, hkv, d, e):
+    """Each request's K and V rows read and written once."""
+    return 2 * 2 * sum(int(c) for c in contexts) * hkv * d * e
+
+
+def cow_bytes(pairs, layers, bs, hkv, d, e):
+    """Every (src, dst) page copied in every layer, K and V, read and written."""
+    return 2 * pairs * 2 * layers * bs * hkv * d * e

@@ -198,7 +198,7 @@ def test_fused_store_with_only_the_new_token(width, split_k, early_kv):
     n, hq, hkv, d, bs = 3, 16, 8, 128, 16
     kernel, _, _ = mi.decode_plan(n, hq, hkv, d, torch.bfloat16, bs, split_k, "cuda", width)
     if "MICROINFER_B200_DECODE" not in os.environ:  # not pinned to one kernel
-        assert kernel == "mma"
+        assert kernel in ("mma", "mma_pair")
     g = torch.Generator(device="cuda").manual_seed(3)
     kc = torch.randn(8, bs, hkv, d, generator=g, device="cuda").to(torch.bfloat16)
     vc = torch.randn_like(kc)
@@ -575,7 +575,7 @@ def test_mma_decode_shapes_match_oracle(dtype, d, g, bs, split, fused):
         at += k
     kernel, _, _ = mi.decode_plan(n, hq, hkv, d, torch_dt, bs, split, "cuda", width)
     if "MICROINFER_B200_DECODE" not in os.environ:
-        assert kernel == "mma"
+        assert kernel in ("mma", "mma_pair")
     kc = (torch.randn(nb, bs, hkv, d, generator=gen) * 0.5).to(torch_dt).cuda()
     vc = (torch.randn(nb, bs, hkv, d, generator=gen) * 0.5).to(torch_dt).cuda()
     q = torch.randn(n, hq, d, generator=gen).to(torch_dt).cuda()
@@ -658,3 +658,51 @@ def test_non_finite_rows_past_the_context_never_reach_the_output(poison, dtype, 
     exp_v = po.dense_varlen_attention(host(qd2, dtype), host(kd[:61], dtype), host(vd[:61], dtype),
                                       cu.numpy(), scale=1 / math.sqrt(d), dtype=dtype)
     assert_close(outv, exp_v, dtype)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("d,g", [(64, 1), (128, 2), (128, 4), (64, 8), (128, 8)])
+@pytest.mark.parametrize("lo,hi", [(1, 40), (100, 600)])
+@pytest.mark.parametrize("fused", [False, True])
+def test_cluster_pair_decode_matches_oracle(dtype, d, g, lo, hi, fused):
+    """Small batches take the cluster-pair plan: two CTAs per (sequence, kv head),
+    every other 16-key chunk each, merged through distributed shared memory.
+    Contexts from 1 key (the second CTA has no chunk at all) up to 600; with the
+    fused store the new token's chunk belongs to either CTA.  Twice in a row."""
+    torch_dt = TORCH[dtype]
+    n, hkv, bs = 5, 4, 16
+    hq = hkv * g
+    gen = torch.Generator().manual_seed(d + g + lo)
+    ctx = torch.randint(lo, hi + 1, (n,), generator=gen, dtype=torch.int32)
+    need = [(int(c) + bs - 1) // bs for c in ctx]
+    nb = sum(need) + 3
+    width = max(need)
+    table = torch.full((n, width), -1, dtype=torch.int32)
+    perm = torch.randperm(nb, generator=gen).to(torch.int32)
+    at = 0
+    for r, k in enumerate(need):
+        table[r, :k] = perm[at:at + k]
+        at += k
+    kernel, split, ws = mi.decode_plan(n, hq, hkv, d, torch_dt, bs, 0, "cuda", width)
+    if "MICROINFER_B200_DECODE" in os.environ or os.environ.get("MICROINFER_B200_DECODE_PAIR") == "0":
+        pytest.skip("kernel pinned")
+    assert (kernel, split, ws) == ("mma_pair", 2, 0)
+    kc = (torch.randn(nb, bs, hkv, d, generator=gen) * 0.5).to(torch_dt).cuda()
+    vc = (torch.randn(nb, bs, hkv, d, generator=gen) * 0.5).to(torch_dt).cuda()
+    table_d, ctx_d = table.cuda(), ctx.cuda()
+    for rep in range(2):
+        q = torch.randn(n, hq, d, generator=gen).to(torch_dt).cuda()
+        if fused:
+            kn = (torch.randn(n, hkv, d, generator=gen) * 0.5).to(torch_dt).cuda()
+            vn = (torch.randn(n, hkv, d, generator=gen) * 0.5).to(torch_dt).cuda()
+            pos = (ctx - 1).long()
+            slots = (table[torch.arange(n), pos // bs].long() * bs + pos % bs).to(torch.int32)
+            out = mi.paged_decode_store(q, kc, vc, table_d, ctx_d, kn, vn, slots.cuda(),
+                                        early_kv=rep == 1)
+        else:
+            out = mi.paged_decode(q, kc, vc, table_d, ctx_d)
+        torch.cuda.synchronize()
+        expected = po.paged_decode(host(q, dtype), host(kc, dtype), host(vc, dtype),
+                                   table.numpy(), ctx.numpy(), scale=1.0 / math.sqrt(d),
+                                   dtype=dtype)
+        assert_close(out, expected, dtype)
