@@ -59,9 +59,10 @@ struct MmaCfg {
   static constexpr int kSmemStages = kWarpsM * kStagesM * kStageBytes;
   static constexpr int kSmemPT = kWarpsM * 256;   // per warp: P^T of a chunk, [16 keys][8 queries]
   static constexpr int kSmemBars = kWarpsM * kStagesM * 8;
-  // cluster pair: the second CTA's merged state, (m, l) then acc, for up to 8 heads
+  static constexpr int kSmem = kSmemStages + kSmemPT + kSmemBars + 16 + 1024;  // + slack
+  // cluster pair: + the second CTA's merged state, (m, l) then acc, for up to 8 heads
   static constexpr int kSmemX = 8 * (D + 2) * 4;
-  static constexpr int kSmem = kSmemStages + kSmemPT + kSmemBars + 16 + kSmemX + 1024;  // + slack
+  static constexpr int kSmemPair = kSmem + kSmemX;
   static_assert(kWarpsM * 8 * (D + 2) * 4 <= kSmemStages, "merge buffers alias the ring");
 };
 
@@ -560,16 +561,17 @@ cudaError_t launch_mma_tdgp(const DecodeMmaParams &P, int64_t num_seqs, int nspl
                             cudaStream_t stream) {
   using C = MmaCfg<D>;
   auto kern = paged_decode_mma_kernel<T, D, G, kPair>;
+  constexpr int smem = kPair ? C::kSmemPair : C::kSmem;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr_set[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
   const dim3 grid(kPair ? 2 : nsplit, P.d.num_kv_heads, static_cast<unsigned>(num_seqs));
-  return launch_pdl(kern, grid, dim3(kWarpsM * 32), C::kSmem, stream, kPair ? 2u : 1u, P);
+  return launch_pdl(kern, grid, dim3(kWarpsM * 32), smem, stream, kPair ? 2u : 1u, P);
 }
 
 template <typename T, int D, int G>

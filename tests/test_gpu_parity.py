@@ -280,7 +280,8 @@ def test_mma_plan_takes_one_split_past_half_the_sms():
     kernel, split, ws = mi.decode_plan(n, 16, 8, 128, torch.bfloat16, 16, 0, "cuda", 32)
     assert (kernel, split, ws) == ("mma", 1, 0)
     kernel, split, _ = mi.decode_plan(8, 16, 8, 128, torch.bfloat16, 16, 0, "cuda", 256)
-    assert kernel == "mma" and split >= 2  # small batch, 4096-key tables: splits
+    # small batch, 4096-key tables: two splits, as a cluster pair (no workspace)
+    assert kernel == "mma_pair" and split == 2
 
 
 @pytest.mark.parametrize("width", [40, 160])  # 640 / 2560-key table bound
