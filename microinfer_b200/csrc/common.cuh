@@ -96,6 +96,18 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// max(a, b, c) in one instruction (three-input max, sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+  float r;
+  asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // ---------------------------------------------------------------------------
 // device status word
 // ---------------------------------------------------------------------------

@@ -52,13 +52,14 @@ struct __align__(64) PrefillTcParams {
   // launched right after this one, which may start once every CTA here has passed
   // its dependency wait (so the trigger comes early).
   int32_t skip_single;
-  // prefill_tc2_kernel's 1-D grid: work units (seq, kv head, tile pair) in the
+  // prefill_tc2_kernel's work items: units (seq, kv head, tile pair) in the
   // order tile pair, kv head, sequence; units from split_from on run as two
-  // single-tile CTAs each, so a last wave that would be less than half full
-  // of pairs becomes one wave of single tiles.
+  // single-tile items each, so a last round that would be less than half full
+  // of pairs becomes one round of single tiles.
   int32_t pairs_per_seq;
   int32_t num_kv_heads;
   int64_t split_from;
+  int64_t num_items;  // pair units before split_from, single tiles from there on
 };
 
 namespace {
@@ -91,14 +92,23 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// Two query tiles per CTA (prefill_tc2_kernel).
+// Two query tiles per work item, persistent CTAs (prefill_tc2_kernel).
 //
-// CTA = (tile pair, kv head, sequence): query tiles A (tokens t0 .. t0+TQ-1)
-// and B (the next TQ tokens) of one kv head share every K/V tile, so each key
-// tile crosses into the SM once for 256 query rows.  352 threads:
+// Work item = (tile pair, kv head, sequence): query tiles A (tokens t0 ..
+// t0+TQ-1) and B (the next TQ tokens) of one kv head share every K/V tile, so
+// each key tile crosses into the SM once for 256 query rows.  Items from
+// split_from on are single tiles (halves of the last pairs), so the last round
+// of items is not half empty.  One CTA per SM takes items blockIdx.x,
+// blockIdx.x + gridDim.x, ...; barriers, TMEM and the rings stay up across
+// items, so the next item's Q and K/V loads and its first S = Q.K^T products
+// run while the previous item's last P.V and output are still in flight (a
+// CTA per item paid ~10 us of setup, ramp and drain on every item).
+// 352 threads:
 //   warps 0-3   softmax of tile A, warps 4-7 softmax of tile B: one TMEM lane
-//               (= query row) per thread, the whole 128-key row in registers
-//   warp 8      TMA: Q of both tiles, then the K tiles (3-stage ring)
+//               (= query row) per thread, the whole 128-key row in registers;
+//               then the item's output rows
+//   warp 8      TMA: Q of both tiles (once the previous item's last S has
+//               read Q), then the K tiles (3-stage ring)
 //   warp 9      TMEM owner and single-thread MMA issuer
 //   warp 10     TMA: the V tiles (2-stage ring)
 // TMEM (512 columns): S_A at 0, S_B at 128, O_A at 256, O_B at 384.  The
@@ -109,7 +119,13 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
 // so one tile's softmax runs while the tensor core works for the other.
 // tcgen05.mma ops of one thread run in issue order: S_X(j+1) overwrites P_X(j)
 // only after PV_X(j) has read it, and once S_X(j+1) is complete PV_X(j) is
-// too, so the softmax may rescale O_X right after S_X(j+1) is ready.
+// too, so the softmax may rescale O_X right after S_X(j+1) is ready.  The
+// first P.V of an item (which overwrites O_X) waits until the softmax warps
+// of tile X have read the previous item's O_X.
+//
+// Every barrier phase is counted per role across items (ring slots, S/P/O
+// handoffs per tile, Q, the V fix-up), so the parities agree without any
+// per-item reset.
 namespace {
 
 constexpr int kThreads2 = 352;
@@ -120,22 +136,75 @@ constexpr int kOffBar2 = kOffV2 + kVStages * kTileBytes;
 constexpr int kSmemBytes2 = kOffBar2 + 256 + 1024;
 
 enum {
-  C_Q = 0,
-  C_KFULL = 1,   // +K stage (3)
-  C_KEMPTY = 4,  // +K stage
-  C_VFULL = 7,   // +V stage (2)
-  C_VEMPTY = 9,  // +V stage
-  C_SFULL = 11,  // +tile: S_X(j) (and everything issued before it) done
-  C_PFULL = 13,  // +tile: P_X(j) in TMEM (128 softmax threads)
-  C_ODONE = 15,  // every MMA done
-  C_FIN = 16,
-  C_VFIX = 17,   // rows past the context in the last V group zeroed (32 lanes of warp 10)
-  C_COUNT = 18
+  C_Q = 0,       // Q of the current item landed
+  C_QEMPTY = 1,  // the item's last S MMA completed: Q may be overwritten
+  C_KFULL = 2,   // +K stage (3)
+  C_KEMPTY = 5,  // +K stage
+  C_VFULL = 8,   // +V stage (2)
+  C_VEMPTY = 10, // +V stage
+  C_SFULL = 12,  // +tile: S_X(j) (and everything issued before it) done
+  C_PFULL = 14,  // +tile: P_X(j) in TMEM (128 softmax threads)
+  C_ODONE = 16,  // +tile: the item's last MMA done, O_X final
+  C_OEMPTY = 18, // +tile: the item's O_X read out (128 softmax threads)
+  C_FIN = 20,
+  // +V stage: rows past the context in the tile's last group zeroed (32 lanes of
+  // warp 10).  One per ring slot: a slot is refilled only after the MMA issuer has
+  // released it, so a slot's fix-ups never run two phases ahead of the issuer.
+  C_VFIX = 21,
+  C_COUNT = 23
 };
 
 // Warp-uniform: this lane's wait succeeded in every lane and nobody aborted.
 __device__ __forceinline__ bool warp_all_ok(bool ok, const int *abort_flag) {
   return __all_sync(0xffffffffu, ok && !*(volatile const int *)abort_flag);
+}
+
+__device__ __forceinline__ bool aborted(const int *abort_flag) {
+  return *(volatile const int *)abort_flag != 0;
+}
+
+// One work item, as every role sees it.
+struct Item {
+  int64_t seq;
+  int kvh, t0, q_start, q_len, kv0, ctx, prefix;
+  int nt[2], nkv_t[2], nkv;
+  int fix_tile, fix_group, fix_valid;
+  bool skip;  // nothing to do (a sequence with fewer tile pairs, or a decode row)
+};
+
+template <int G>
+__device__ __forceinline__ Item item_at(const PrefillTcParams &p, int64_t idx) {
+  constexpr int TQ = 128 / G;
+  Item it;
+  const bool single = idx >= p.split_from;
+  const int64_t unit = single ? p.split_from + (idx - p.split_from) / 2 : idx;
+  const int half = single ? static_cast<int>((idx - p.split_from) & 1) : 0;
+  const int pair = static_cast<int>(unit % p.pairs_per_seq);
+  it.kvh = static_cast<int>((unit / p.pairs_per_seq) % p.num_kv_heads);
+  it.seq = unit / (static_cast<int64_t>(p.pairs_per_seq) * p.num_kv_heads);
+  it.q_start = __ldg(p.cu_q + it.seq);
+  it.q_len = __ldg(p.cu_q + it.seq + 1) - it.q_start;
+  it.t0 = pair * 2 * TQ + half * TQ;
+  it.skip = it.t0 >= it.q_len || (p.skip_single && it.q_len == 1);
+  it.kv0 = __ldg(p.cu_k + it.seq);
+  it.ctx = __ldg(p.cu_k + it.seq + 1) - it.kv0;
+  it.prefix = it.ctx - it.q_len;
+  it.nt[0] = it.skip ? 0 : min(TQ, it.q_len - it.t0);
+  it.nt[1] = it.skip || single ? 0 : max(0, min(TQ, it.q_len - it.t0 - TQ));
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const int maxpos = it.prefix + it.t0 + x * TQ + it.nt[x] - 1;
+    it.nkv_t[x] = it.nt[x] > 0 && maxpos >= 0 ? maxpos / 128 + 1 : 0;
+  }
+  it.nkv = max(it.nkv_t[0], it.nkv_t[1]);
+  // The last key tile may hold a partial 16-key group (rows ctx % 16 .. 15 of
+  // it lie past the context and hold stale pool contents, or another
+  // sequence's rows in dense mode).  They meet P = 0, but 0 * Inf or NaN is
+  // NaN, so the V producer zeroes them before P.V reads that tile.
+  it.fix_tile = (it.nkv > 0 && it.ctx % 16 != 0 && (it.ctx - 1) / 128 == it.nkv - 1) ? it.nkv - 1 : -1;
+  it.fix_group = ((it.ctx - 1) % 128) / 16;
+  it.fix_valid = it.ctx % 16;
+  return it;
 }
 
 }  // namespace
@@ -157,52 +226,12 @@ __global__ void __launch_bounds__(kThreads2, 1)
   const uint32_t sQ = smem_addr(smem + kOffQ2);
   const uint32_t sK = smem_addr(smem + kOffK2);
   const uint32_t sV = smem_addr(smem + kOffV2);
-
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t cta = blockIdx.x;
-  const bool single = cta >= p.split_from;
-  const int64_t unit = single ? p.split_from + (cta - p.split_from) / 2 : cta;
-  const int half = single ? static_cast<int>((cta - p.split_from) & 1) : 0;
-  const int pair = static_cast<int>(unit % p.pairs_per_seq);
-  const int kvh = static_cast<int>((unit / p.pairs_per_seq) % p.num_kv_heads);
-  const int64_t seq = unit / (static_cast<int64_t>(p.pairs_per_seq) * p.num_kv_heads);
-
-  pdl_wait();
-  if (p.skip_single) pdl_launch_dependents();
-  const int q_start = p.cu_q[seq];
-  const int q_len = p.cu_q[seq + 1] - q_start;
-  const int t0 = pair * 2 * TQ + half * TQ;
-  if (t0 >= q_len) return;  // uniform: this sequence has fewer tile pairs
-  if (p.skip_single && q_len == 1) return;  // a decode row: the decode launch handles it
-  const int kv0 = p.cu_k[seq];
-  const int ctx = p.cu_k[seq + 1] - kv0;
-  const int prefix = ctx - q_len;
-  const int nt[2] = {min(TQ, q_len - t0), single ? 0 : max(0, min(TQ, q_len - t0 - TQ))};
-  int nkv_t[2];
-#pragma unroll
-  for (int x = 0; x < 2; ++x) {
-    const int maxpos = prefix + t0 + x * TQ + nt[x] - 1;
-    nkv_t[x] = nt[x] > 0 && maxpos >= 0 ? maxpos / 128 + 1 : 0;
-  }
-  const int nkv = max(nkv_t[0], nkv_t[1]);
-  // The last key tile may hold a partial 16-key group (rows ctx % 16 .. 15 of
-  // it lie past the context and hold stale pool contents, or another
-  // sequence's rows in dense mode).  They meet P = 0, but 0 * Inf or NaN is
-  // NaN, so the V producer zeroes them before P.V reads that tile.
-  const int fix_tile = (ctx % 16 != 0 && (ctx - 1) / 128 == nkv - 1) ? nkv - 1 : -1;
-  const int fix_group = ((ctx - 1) % 128) / 16, fix_valid = ctx % 16;
   T *out = static_cast<T *>(p.out);
-  if (nkv == 0) {  // no visible key (context shorter than the chunk): zeros, as the generic kernel
-    for (int i = threadIdx.x; i < (nt[0] + nt[1]) * G * 128; i += kThreads2) {
-      const int row = i / 128, d = i % 128;
-      out[(static_cast<int64_t>(q_start + t0 + row / G) * p.num_q_heads + kvh * G + row % G) * 128 + d] =
-          Elem<T>::from_float(0.f);
-    }
-    return;
-  }
 
   if (threadIdx.x == 0) {
     mbar_init(&bar[C_Q], 1);
+    mbar_init(&bar[C_QEMPTY], 1);
     for (int s = 0; s < kKStages; ++s) {
       mbar_init(&bar[C_KFULL + s], 1);
       mbar_init(&bar[C_KEMPTY + s], 1);
@@ -214,10 +243,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bar[C_SFULL + x], 1);
       mbar_init(&bar[C_PFULL + x], 128);
+      mbar_init(&bar[C_ODONE + x], 1);
+      mbar_init(&bar[C_OEMPTY + x], 128);
     }
-    mbar_init(&bar[C_ODONE], 1);
     mbar_init(&bar[C_FIN], 1);
-    mbar_init(&bar[C_VFIX], 32);
+    for (int s = 0; s < kVStages; ++s) mbar_init(&bar[C_VFIX + s], 32);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -227,146 +257,197 @@ __global__ void __launch_bounds__(kThreads2, 1)
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
 
+  pdl_wait();
+  if (p.skip_single) pdl_launch_dependents();
+  const int64_t n_items = p.num_items;
+
   if (warp == 8 || warp == 10) {
     // ---------------------------------------------------------- producers
-    // warp 8 loads Q and the K tiles, warp 10 the V tiles.  Table lookups as in
-    // prefill_tc_kernel: batches of 4 tiles, one batch ahead.
+    // warp 8 loads Q and the K tiles, warp 10 the V tiles.  Block-table
+    // lookups in batches of 4 tiles, one batch ahead.
     const bool is_v = warp == 10;
-    const int32_t *table = p.block_tables + seq * p.bt_stride;
-    auto kv_entry = [&](int key0) -> int {
-      if (key0 >= ctx || !p.paged) return 0;
-      const int64_t col = key0 / p.block_size;
-      return col < p.bt_stride ? __ldg(table + col) : -1;
-    };
-    auto kv_row = [&](int key0, int entry) -> int {
-      if (key0 >= ctx) return static_cast<int>(p.kv_rows);  // past the context: zero fill
-      if (!p.paged) return kv0 + key0;
-      if (entry < 0 || entry >= p.num_blocks) {
-        flag_status(p.status, MI_DEV_BAD_BLOCK);
-        return static_cast<int>(p.kv_rows);
-      }
-      return static_cast<int>(static_cast<int64_t>(entry) * p.block_size + key0 % p.block_size);
-    };
-    bool ok = true;
-    int armed = 0;
-    if (lane == 0) {
-      tc::prefetch_tmap(is_v ? &p.tmap_v : &p.tmap_k);
-      if (!is_v) {
-        tc::prefetch_tmap(&p.tmap_q);
-        const int ntiles = nt[1] > 0 ? 2 : 1;
-        mbar_arrive_expect_tx(&bar[C_Q], ntiles * 2 * kHalf);
-        for (int x = 0; x < ntiles; ++x)
-          for (int dh = 0; dh < 2; ++dh)
-            tc::tma_load_3d(smem + kOffQ2 + x * kTileBytes + dh * kHalf, &p.tmap_q, dh * 64, kvh * G,
-                            q_start + t0 + x * TQ, &bar[C_Q]);
-      }
-    }
-    const int g = lane >> 1, dh = lane & 1;
     const int nst = is_v ? kVStages : kKStages;
     const CUtensorMap *map = is_v ? &p.tmap_v : &p.tmap_k;
     uint8_t *ring = smem + (is_v ? kOffV2 : kOffK2);
     const int full0 = is_v ? C_VFULL : C_KFULL, empty0 = is_v ? C_VEMPTY : C_KEMPTY;
+    const int g = lane >> 1, dh = lane & 1;
     const int bt = lane >> 3, bg = lane & 7;
-    auto entry_for = [&](int tile) { return tile < nkv ? kv_entry(tile * 128 + bg * 16) : 0; };
-    int cur = entry_for(bt), nxt = entry_for(4 + bt);
-    for (int j = 0; j < nkv && ok; ++j) {
-      const int s = j % nst;
-      const uint32_t empty_parity = ((j / nst) & 1) ^ 1;
-      if (j > 0 && (j & 3) == 0) {
-        cur = nxt;
-        nxt = entry_for(j + 4 + bt);
-      }
-      const int entry = __shfl_sync(0xffffffffu, cur, ((j & 3) * 8 + g) & 31);
-      const int row = lane < 16 ? kv_row(j * 128 + g * 16, entry) : 0;
-      int good = 1;
-      if (lane == 0)
-        good = mbar_wait_bounded(&bar[empty0 + s], empty_parity, p.status) && !*(volatile int *)abort_flag;
-      good = __shfl_sync(0xffffffffu, good, 0);
-      if (!good) {
-        ok = false;
-        break;
-      }
-      if (lane == 0) mbar_arrive_expect_tx(&bar[full0 + s], kTileBytes);
-      __syncwarp();
-      if (lane < 16)
-        tc::tma_load_3d(ring + s * kTileBytes + dh * kHalf + g * 2048, map, dh * 64, kvh, row, &bar[full0 + s]);
-      armed = j + 1;
-      if (is_v && j == fix_tile) {
-        // Wait for the tile, zero the group's rows past the context (both 64-column
-        // halves; whole 128-byte rows, so the swizzle does not matter), make the
-        // writes visible to the tensor core and release the tile to the MMA issuer.
-        int landed = 1;
-        if (lane == 0) landed = mbar_wait_bounded(&bar[full0 + s], (j / nst) & 1, p.status);
-        landed = __shfl_sync(0xffffffffu, landed, 0);
-        if (landed) {
-          uint8_t *grp = ring + s * kTileBytes + fix_group * 2048;
-          for (int i = lane; i < (16 - fix_valid) * 16; i += 32) {
-            const int rr = fix_valid + i / 16, c = i % 16;
-            *reinterpret_cast<uint4 *>(grp + (c >> 3) * kHalf + rr * 128 + (c & 7) * 16) =
-                make_uint4(0u, 0u, 0u, 0u);
-          }
-        } else {
-          ok = false;
+    if (lane == 0) {
+      tc::prefetch_tmap(map);
+      if (!is_v) tc::prefetch_tmap(&p.tmap_q);
+    }
+    bool ok = true;
+    uint32_t tiles = 0;  // tiles issued by this warp so far (ring position)
+    uint32_t items_q = 0;
+    for (int64_t idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+      const Item it = item_at<G>(p, idx);
+      if (it.skip || it.nkv == 0) continue;
+      const int32_t *table = p.block_tables + it.seq * p.bt_stride;
+      auto kv_entry = [&](int key0) -> int {
+        if (key0 >= it.ctx || !p.paged) return 0;
+        const int64_t col = key0 / p.block_size;
+        return col < p.bt_stride ? __ldg(table + col) : -1;
+      };
+      auto kv_row = [&](int key0, int entry) -> int {
+        if (key0 >= it.ctx) return static_cast<int>(p.kv_rows);  // past the context: zero fill
+        if (!p.paged) return it.kv0 + key0;
+        if (entry < 0 || entry >= p.num_blocks) {
+          flag_status(p.status, MI_DEV_BAD_BLOCK);
+          return static_cast<int>(p.kv_rows);
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(&bar[C_VFIX]);
+        return static_cast<int>(static_cast<int64_t>(entry) * p.block_size + key0 % p.block_size);
+      };
+      if (!is_v) {  // Q of both tiles, once the previous item's S products have read Q
+        int good = 1;
+        if (lane == 0)
+          good = mbar_wait_bounded(&bar[C_QEMPTY], (items_q & 1) ^ 1, p.status) && !aborted(abort_flag);
+        if (!__shfl_sync(0xffffffffu, good, 0)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          const int ntiles = it.nt[1] > 0 ? 2 : 1;
+          mbar_arrive_expect_tx(&bar[C_Q], ntiles * 2 * kHalf);
+          for (int x = 0; x < ntiles; ++x)
+            for (int h = 0; h < 2; ++h)
+              tc::tma_load_3d(smem + kOffQ2 + x * kTileBytes + h * kHalf, &p.tmap_q, h * 64,
+                              it.kvh * G, it.q_start + it.t0 + x * TQ, &bar[C_Q]);
+        }
+        ++items_q;
+      }
+      auto entry_for = [&](int tile) { return tile < it.nkv ? kv_entry(tile * 128 + bg * 16) : 0; };
+      int cur = entry_for(bt), nxt = entry_for(4 + bt);
+      for (int j = 0; j < it.nkv; ++j) {
+        const uint32_t s = tiles % nst;
+        const uint32_t empty_parity = ((tiles / nst) & 1) ^ 1;
+        if (j > 0 && (j & 3) == 0) {
+          cur = nxt;
+          nxt = entry_for(j + 4 + bt);
+        }
+        const int entry = __shfl_sync(0xffffffffu, cur, ((j & 3) * 8 + g) & 31);
+        const int row = lane < 16 ? kv_row(j * 128 + g * 16, entry) : 0;
+        int good = 1;
+        if (lane == 0)
+          good = mbar_wait_bounded(&bar[empty0 + s], empty_parity, p.status) && !aborted(abort_flag);
+        if (!__shfl_sync(0xffffffffu, good, 0)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) mbar_arrive_expect_tx(&bar[full0 + s], kTileBytes);
+        __syncwarp();
+        if (lane < 16)
+          tc::tma_load_3d(ring + s * kTileBytes + dh * kHalf + g * 2048, map, dh * 64, it.kvh, row,
+                          &bar[full0 + s]);
+        if (is_v && j == it.fix_tile) {
+          // Wait for the tile, zero the group's rows past the context (both 64-column
+          // halves; whole 128-byte rows, so the swizzle does not matter), make the
+          // writes visible to the tensor core and release the tile to the MMA issuer.
+          int landed = 1;
+          if (lane == 0) landed = mbar_wait_bounded(&bar[full0 + s], (tiles / nst) & 1, p.status);
+          landed = __shfl_sync(0xffffffffu, landed, 0);
+          if (landed) {
+            uint8_t *grp = ring + s * kTileBytes + it.fix_group * 2048;
+            for (int i = lane; i < (16 - it.fix_valid) * 16; i += 32) {
+              const int rr = it.fix_valid + i / 16, c = i % 16;
+              *reinterpret_cast<uint4 *>(grp + (c >> 3) * kHalf + rr * 128 + (c & 7) * 16) =
+                  make_uint4(0u, 0u, 0u, 0u);
+            }
+          } else {
+            ok = false;
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          mbar_arrive(&bar[C_VFIX + s]);
+        }
+        ++tiles;
+        if (!ok) break;
       }
     }
     if (!ok && lane == 0) {
       *(volatile int *)abort_flag = 1;
       // Let this CTA's own loads in flight land before its shared memory goes away.
-      for (int j = max(0, armed - nst); j < armed; ++j)
-        mbar_wait_bounded(&bar[full0 + j % nst], (j / nst) & 1, p.status);
+      const uint32_t lo = tiles > static_cast<uint32_t>(nst) ? tiles - nst : 0;
+      for (uint32_t t = lo; t < tiles; ++t)
+        mbar_wait_bounded(&bar[full0 + t % nst], (t / nst) & 1, p.status);
+      if (!is_v && items_q > 0) mbar_wait_bounded(&bar[C_Q], (items_q - 1) & 1, p.status);
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      auto s_mma = [&](int x, int j) {  // S_X(j) = Q_X K_j^T
-        const int ks = j % kKStages;
+      uint32_t kt = 0, vt = 0;            // K / V tiles consumed (ring positions)
+      uint32_t sc[2] = {0, 0};            // S_X products issued
+      uint32_t uses[2] = {0, 0};          // items that used tile X
+      uint32_t items_q = 0;
+      uint32_t fixes[kVStages] = {0, 0};  // fix-ups consumed per V ring slot
+      bool ok = true;
+      auto s_mma = [&](int x) {  // S_X = Q_X K^T with the K tile at ring position kt
+        const uint32_t ks = kt % kKStages;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           tc::umma_f16(tmem + x * 128, kmajor_desc(sQ + x * kTileBytes, kk),
                        kmajor_desc(sK + ks * kTileBytes, kk), kIdescQK, kk > 0 ? 1u : 0u);
         tc::umma_commit(&bar[C_SFULL + x]);
+        ++sc[x];
       };
       auto pv_mma = [&](int x, int j) -> bool {  // O_X += P_X(j) V_j, P from TMEM
-        if (!mbar_spin_bounded(&bar[C_PFULL + x], j & 1, p.status)) return false;
+        if (!mbar_spin_bounded(&bar[C_PFULL + x], (sc[x] - 1) & 1, p.status)) return false;
         tc::fence_after_sync();
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           tc::umma_f16_tmem_a(tmem + 256 + x * 128, tmem + x * 128 + kk * 8,
-                              mnmajor_desc(sV + (j % kVStages) * kTileBytes, kk), kIdescPV,
+                              mnmajor_desc(sV + (vt % kVStages) * kTileBytes, kk), kIdescPV,
                               (j > 0 || kk > 0) ? 1u : 0u);
         return true;
       };
-      bool ok = mbar_spin_bounded(&bar[C_Q], 0, p.status) &&
-                mbar_spin_bounded(&bar[C_KFULL], 0, p.status) && !*(volatile int *)abort_flag;
-      if (ok) {
-        tc::fence_after_sync();
-        if (nkv_t[0] > 0) s_mma(0, 0);
-        if (nkv_t[1] > 0) s_mma(1, 0);
-        tc::umma_commit(&bar[C_KEMPTY]);
-      }
-      for (int j = 0; j < nkv && ok; ++j) {
-        const bool nA = j + 1 < nkv_t[0], nB = j + 1 < nkv_t[1];
-        const int vs = j % kVStages, ks = (j + 1) % kKStages;
-        ok = mbar_spin_bounded(&bar[C_VFULL + vs], (j / kVStages) & 1, p.status) &&
-             (!(nA || nB) || mbar_spin_bounded(&bar[C_KFULL + ks], ((j + 1) / kKStages) & 1, p.status)) &&
-             !*(volatile int *)abort_flag;
-        if (ok && j == fix_tile) ok = mbar_spin_bounded(&bar[C_VFIX], 0, p.status);
+      for (int64_t idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+        const Item it = item_at<G>(p, idx);
+        if (it.skip || it.nkv == 0) continue;
+        const bool use0 = it.nkv_t[0] > 0, use1 = it.nkv_t[1] > 0;
+        ok = mbar_spin_bounded(&bar[C_Q], items_q & 1, p.status) &&
+             mbar_spin_bounded(&bar[C_KFULL + kt % kKStages], (kt / kKStages) & 1, p.status) &&
+             !aborted(abort_flag);
+        ++items_q;
         if (!ok) break;
         tc::fence_after_sync();
-        if (j < nkv_t[0] && !(ok = pv_mma(0, j))) break;
-        if (nA) s_mma(0, j + 1);
-        if (j < nkv_t[1] && !(ok = pv_mma(1, j))) break;
-        if (nB) s_mma(1, j + 1);
-        if (nA || nB) tc::umma_commit(&bar[C_KEMPTY + ks]);
-        tc::umma_commit(&bar[C_VEMPTY + vs]);
+        if (use0) s_mma(0);
+        if (use1) s_mma(1);
+        tc::umma_commit(&bar[C_KEMPTY + kt % kKStages]);
+        ++kt;
+        if (it.nkv == 1) tc::umma_commit(&bar[C_QEMPTY]);
+        for (int j = 0; j < it.nkv && ok; ++j) {
+          const bool nA = j + 1 < it.nkv_t[0], nB = j + 1 < it.nkv_t[1];
+          ok = mbar_spin_bounded(&bar[C_VFULL + vt % kVStages], (vt / kVStages) & 1, p.status) &&
+               (!(nA || nB) ||
+                mbar_spin_bounded(&bar[C_KFULL + kt % kKStages], (kt / kKStages) & 1, p.status)) &&
+               !aborted(abort_flag);
+          if (ok && j == it.fix_tile) {
+            const uint32_t vs = vt % kVStages;
+            ok = mbar_spin_bounded(&bar[C_VFIX + vs], fixes[vs]++ & 1, p.status);
+          }
+          // The first P.V of a tile overwrites O_X: the previous item's O_X must be read out.
+          if (ok && j == 0 && use0) ok = mbar_spin_bounded(&bar[C_OEMPTY], (uses[0] & 1) ^ 1, p.status);
+          if (ok && j == 0 && use1) ok = mbar_spin_bounded(&bar[C_OEMPTY + 1], (uses[1] & 1) ^ 1, p.status);
+          if (!ok) break;
+          tc::fence_after_sync();
+          if (j < it.nkv_t[0] && !(ok = pv_mma(0, j))) break;
+          if (nA) s_mma(0);
+          if (j < it.nkv_t[1] && !(ok = pv_mma(1, j))) break;
+          if (nB) s_mma(1);
+          if (nA || nB) {
+            tc::umma_commit(&bar[C_KEMPTY + kt % kKStages]);
+            ++kt;
+            if (j + 2 == it.nkv) tc::umma_commit(&bar[C_QEMPTY]);  // the item's last S issued
+          }
+          tc::umma_commit(&bar[C_VEMPTY + vt % kVStages]);
+          ++vt;
+        }
+        if (!ok) break;
+        if (use0) tc::umma_commit(&bar[C_ODONE]);
+        if (use1) tc::umma_commit(&bar[C_ODONE + 1]);
+        uses[0] += use0 ? 1 : 0;
+        uses[1] += use1 ? 1 : 0;
       }
       if (!ok) *(volatile int *)abort_flag = 1;
-      // Every MMA issued by this thread completes before the epilogue reads O
-      // and before TMEM is released.
-      tc::umma_commit(&bar[C_ODONE]);
+      // Every MMA issued by this thread completes before TMEM is released.
       tc::umma_commit(&bar[C_FIN]);
       mbar_spin_bounded(&bar[C_FIN], 0, p.status);
     }
@@ -377,108 +458,116 @@ __global__ void __launch_bounds__(kThreads2, 1)
     const int q4 = warp & 3;
     const int r = q4 * 32 + lane;  // TMEM lane = query row of the tile
     const int tok = r / G;
-    const bool rvalid = tok < nt[x];
-    const int pos = prefix + t0 + x * TQ + tok;
-    const int my_nkv = nkv_t[x];
     const uint32_t lane_off = static_cast<uint32_t>(q4 * 32) << 16;
     const uint32_t tS = tmem + x * 128 + lane_off, tO = tmem + 256 + x * 128 + lane_off;
     const float sl2 = p.scale_log2;
     const bool pos_scale = sl2 >= 0.f;
     const float masked = pos_scale ? -INFINITY : INFINITY;
-    float m = -INFINITY, l = 0.f;
+    uint32_t sc = 0, uses = 0;  // S_X tiles consumed, items that used tile X
     bool ok = true;
-    for (int j = 0; j < my_nkv; ++j) {
-      if (!warp_all_ok(mbar_wait_bounded(&bar[C_SFULL + x], j & 1, p.status), abort_flag)) {
-        ok = false;
-        break;
-      }
-      tc::fence_after_sync();
-      // The whole row in registers: one TMEM round trip per tile.
-      float sr[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float v[32];
-        tc::tmem_ld32(tS + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sr[c * 32 + i] = v[i];
-      }
-      tc::tmem_wait_ld();
-      // key c of the tile is visible iff c <= pos - j * 128: only diagonal
-      // tiles (and rows past the chunk) mask anything.
-      const int lim = rvalid ? pos - j * 128 : -1;
-      if (lim < 127) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) sr[c] = c <= lim ? sr[c] : masked;
-      }
-      float r4[4] = {masked, masked, masked, masked};
-      if (pos_scale) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) r4[c & 3] = fmaxf(r4[c & 3], sr[c]);
-      } else {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) r4[c & 3] = fminf(r4[c & 3], sr[c]);
-      }
-      const float best = pos_scale ? fmaxf(fmaxf(r4[0], r4[1]), fmaxf(r4[2], r4[3]))
-                                   : fminf(fminf(r4[0], r4[1]), fminf(r4[2], r4[3]));
-      const float mx = lim < 0 ? -INFINITY : best * sl2;  // row max, log2 domain
-      float m_new = m, alpha = 1.f;
-      bool rescale = false;
-      if (mx > m + 8.f) {
-        m_new = mx;
-        rescale = m != -INFINITY;
-        alpha = rescale ? fast_exp2(m - m_new) : 0.f;
-      }
-      // P = 2^(s * scale - m) as 16-bit pairs over the first 64 columns of S
-      // (the row is already read back).
-      const float nb = m_new == -INFINITY ? 0.f : -m_new;  // masked: ex2(-inf) = 0
-      const float2 sc2 = make_float2(sl2, sl2), nb2 = make_float2(nb, nb);
-      float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {  // keys 16q .. 16q+15 -> columns 8q .. 8q+7
-        float pk[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float2 a2 = ffma2(make_float2(sr[q * 16 + 2 * i], sr[q * 16 + 2 * i + 1]), sc2, nb2);
-          const float2 e = make_float2(fast_exp2(a2.x), fast_exp2(a2.y));
-          sum2[i & 1] = fadd2(sum2[i & 1], e);
-          pk[i] = __uint_as_float(pack2(e.x, e.y, kBf16));
+    for (int64_t idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
+      const Item it = item_at<G>(p, idx);
+      if (it.skip || it.nt[x] == 0) continue;
+      const bool rvalid = tok < it.nt[x];
+      const int pos = it.prefix + it.t0 + x * TQ + tok;
+      const int my_nkv = it.nkv_t[x];
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < my_nkv; ++j) {
+        if (!warp_all_ok(mbar_wait_bounded(&bar[C_SFULL + x], sc & 1, p.status), abort_flag)) {
+          ok = false;
+          break;
         }
-        tc::tmem_st8(tS + q * 8, pk);
-      }
-      // O_X is quiescent here (PV_X(j-1) completed before S_X(j) did) and
-      // PV_X(j) waits for this thread's arrival below.
-      if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
-        const float ra = rescale ? alpha : 1.f;
-#pragma unroll 1
+        ++sc;
+        tc::fence_after_sync();
+        // The whole row in registers: one TMEM round trip per tile.
+        float sr[128];
+#pragma unroll
         for (int c = 0; c < 4; ++c) {
-          float o[32];
-          tc::tmem_ld32(tO + c * 32, o);
-          tc::tmem_wait_ld();
+          float v[32];
+          tc::tmem_ld32(tS + c * 32, v);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= ra;
-          tc::tmem_st32(tO + c * 32, o);
+          for (int i = 0; i < 32; ++i) sr[c * 32 + i] = v[i];
         }
+        tc::tmem_wait_ld();
+        // key c of the tile is visible iff c <= pos - j * 128: only diagonal
+        // tiles (and rows past the chunk) mask anything.
+        const int lim = rvalid ? pos - j * 128 : -1;
+        if (lim < 127) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) sr[c] = c <= lim ? sr[c] : masked;
+        }
+        float r4[4] = {masked, masked, masked, masked};
+        if (pos_scale) {
+#pragma unroll
+          for (int c = 0; c < 128; c += 2) r4[(c >> 1) & 3] = fmax3(r4[(c >> 1) & 3], sr[c], sr[c + 1]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 128; c += 2) r4[(c >> 1) & 3] = fmin3(r4[(c >> 1) & 3], sr[c], sr[c + 1]);
+        }
+        const float best = pos_scale ? fmaxf(fmaxf(r4[0], r4[1]), fmaxf(r4[2], r4[3]))
+                                     : fminf(fminf(r4[0], r4[1]), fminf(r4[2], r4[3]));
+        const float mx = lim < 0 ? -INFINITY : best * sl2;  // row max, log2 domain
+        float m_new = m, alpha = 1.f;
+        bool rescale = false;
+        if (mx > m + 8.f) {
+          m_new = mx;
+          rescale = m != -INFINITY;
+          alpha = rescale ? fast_exp2(m - m_new) : 0.f;
+        }
+        // P = 2^(s * scale - m) as 16-bit pairs over the first 64 columns of S
+        // (the row is already read back).
+        const float nb = m_new == -INFINITY ? 0.f : -m_new;  // masked: ex2(-inf) = 0
+        const float2 sc2 = make_float2(sl2, sl2), nb2 = make_float2(nb, nb);
+        float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {  // keys 16q .. 16q+15 -> columns 8q .. 8q+7
+          float pk[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float2 a2 = ffma2(make_float2(sr[q * 16 + 2 * i], sr[q * 16 + 2 * i + 1]), sc2, nb2);
+            const float2 e = make_float2(fast_exp2(a2.x), fast_exp2(a2.y));
+            sum2[i & 1] = fadd2(sum2[i & 1], e);
+            pk[i] = __uint_as_float(pack2(e.x, e.y, kBf16));
+          }
+          tc::tmem_st8(tS + q * 8, pk);
+        }
+        // O_X is quiescent here (PV_X(j-1) completed before S_X(j) did) and
+        // PV_X(j) waits for this thread's arrival below.
+        if (j >= 1 && __any_sync(0xffffffffu, rescale)) {
+          const float ra = rescale ? alpha : 1.f;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tc::tmem_ld32(tO + c * 32, o);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= ra;
+            tc::tmem_st32(tO + c * 32, o);
+          }
+        }
+        tc::tmem_wait_st();
+        tc::fence_before_sync();
+        mbar_arrive(&bar[C_PFULL + x]);
+        const float2 s01 = fadd2(sum2[0], sum2[1]);
+        l = l * alpha + (s01.x + s01.y);
+        m = m_new;
       }
-      tc::tmem_wait_st();
-      tc::fence_before_sync();
-      mbar_arrive(&bar[C_PFULL + x]);
-      const float2 s01 = fadd2(sum2[0], sum2[1]);
-      l = l * alpha + (s01.x + s01.y);
-      m = m_new;
-    }
-    if (ok && my_nkv > 0)
-      ok = warp_all_ok(mbar_wait_bounded(&bar[C_ODONE], 0, p.status), abort_flag);
-    if (ok) {
-      tc::fence_after_sync();
+      if (!ok) break;
+      if (my_nkv > 0) {
+        ok = warp_all_ok(mbar_wait_bounded(&bar[C_ODONE + x], uses & 1, p.status), abort_flag);
+        if (!ok) break;
+        tc::fence_after_sync();
+      }
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      T *orow = out + (static_cast<int64_t>(q_start + t0 + x * TQ + tok) * p.num_q_heads + kvh * G + r % G) * 128;
+      T *orow = out + (static_cast<int64_t>(it.q_start + it.t0 + x * TQ + tok) * p.num_q_heads +
+                       it.kvh * G + r % G) * 128;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float o[32];
         if (my_nkv > 0) {
           tc::tmem_ld32(tO + c * 32, o);
           tc::tmem_wait_ld();
-        } else {
+        } else {  // no visible key (context shorter than the chunk): zeros
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = 0.f;
         }
@@ -494,9 +583,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
           }
         }
       }
-    } else if (lane == 0) {
-      *(volatile int *)abort_flag = 1;
+      if (my_nkv > 0) {  // O_X is read: the next item's first P.V may overwrite it
+        tc::fence_before_sync();
+        mbar_arrive(&bar[C_OEMPTY + x]);
+        ++uses;
+      }
     }
+    if (!ok && lane == 0) *(volatile int *)abort_flag = 1;
   }
 
   pdl_launch_dependents();
@@ -534,13 +627,16 @@ cudaError_t launch_tg2(PrefillTcParams &p, int num_kv_heads, int64_t num_seqs, i
   const int64_t pairs = (max_seqlen_q + 2 * TQ - 1) / (2 * TQ);
   const int64_t units = pairs * num_kv_heads * num_seqs;
   const int64_t sms = sm_count_current();
-  const int64_t rem = units % sms;  // pair units of the last (partial) wave
+  const int64_t rem = units % sms;  // pair units of the last (partial) round
   const int64_t split = units > sms && rem > 0 && 2 * rem <= sms ? rem : 0;
   if (units + split > 0x7fffffff) return cudaErrorNotSupported;
   p.pairs_per_seq = static_cast<int32_t>(pairs);
   p.num_kv_heads = num_kv_heads;
   p.split_from = units - split;
-  return launch_pdl(kern, dim3(static_cast<unsigned>(units + split)), dim3(kThreads2), kSmemBytes2, stream, p);
+  p.num_items = units + split;
+  // one persistent CTA per SM (or per item, when there are fewer)
+  const int64_t ctas = p.num_items < sms ? p.num_items : sms;
+  return launch_pdl(kern, dim3(static_cast<unsigned>(ctas)), dim3(kThreads2), kSmemBytes2, stream, p);
 }
 
 }  // namespace
