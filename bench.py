@@ -49,7 +49,7 @@ WORKLOAD = "BASELINE configs[1]: Qwen3-0.6B decode step, bf16, 28 layers, batch 
 DECODE_KERNEL_NAMES = {"mma": "paged_decode_mma_kernel", "simt": "paged_decode_kernel",
                        "mma_pair": "paged_decode_mma_kernel (cluster pairs)",
                        "generic": "attn_generic_kernel"}
-DECODE_PROFILES = {"mma": "decode_mma_qwen3_0.6b_config2.md"}
+DECODE_PROFILES = {"mma_pair": "decode_mma_pair_qwen3_0.6b_config2.md"}
 
 
 def _peaks():
@@ -511,7 +511,9 @@ def measure_prefill(device, workload: str, layers: int = 28, reps: int = 10):
            "kernel": prefill_kernel_name(), "layers": layers,
            "us_per_layer": round(ms_layer * 1e3, 2), "flops_per_layer": flops,
            "tflops": round(tflops, 1), "tensor_frac": round(tflops / peaks["bf16_tflops"], 4),
-           "peak_source": f"bf16_tflops of {src}", "store_tokens": tokens, "checked": check}
+           "peak_source": f"bf16_tflops of {src}", "store_tokens": tokens, "checked": check,
+           "traffic_ncu": (_profiled_traffic("prefill_tc2_shared_prefix.md")
+                           if workload == "prefix" else None)}
     if workload == "mixed":
         t_min = kv_bytes / (peaks["hbm_gbs"] * 1e9) + flops / (peaks["bf16_tflops"] * 1e12)
         res["combined_bound_frac"] = round(t_min / (ms_layer * 1e-3), 4)
@@ -654,6 +656,7 @@ def measure_shared_prefix_step(device, layers: int = LAYERS, decode_steps: int =
                     "full, page 63 shared with 8 tokens), CoW of page 63 per sequence, 128-token "
                     "suffix prefill, 16 decode steps, gather of the 1144-row contexts; 28 layers",
         "cow": {"kernel": "cow_kernel", "pairs": n, "layers": layers,
+                "traffic_ncu": _profiled_traffic("cow_kernel_config4_64pairs_28layers.md"),
                 "us": round(ms_cow * 1e3, 2), "bytes": b_cow,
                 "gbs": round(b_cow / (ms_cow * 1e-3) / 1e9, 1),
                 "hbm_frac": round(b_cow / (ms_cow * 1e-3) / 1e9 / hbm, 4)},
@@ -670,6 +673,7 @@ def measure_shared_prefix_step(device, layers: int = LAYERS, decode_steps: int =
                    "unique_hbm_frac": round(layers * unique / (ms_dec * 1e-3) / 1e9 / hbm, 4),
                    "checked": check_d},
         "gather": {"kernel": "gather_kernel", "us_per_layer": round(ms_gat / layers * 1e3, 2),
+                   "traffic_ncu_1152_rows": _profiled_traffic("gather_kernel_config4_64x1152.md"),
                    "bytes_per_layer": b_gat,
                    "gbs": round(b_gat / (ms_gat / layers * 1e-3) / 1e9, 1),
                    "hbm_frac": round(b_gat / (ms_gat / layers * 1e-3) / 1e9 / hbm, 4)},
@@ -715,6 +719,7 @@ def measure_store(device, layers: int = LAYERS, reps: int = 20):
                       "gbs": round(gbs, 1), "hbm_frac": round(gbs / peaks["hbm_gbs"], 4)}
         del pool, kn, vn
     return {"kernel": "store_kv_vec16_kernel", "checked": "written rows bit-exact",
+            "traffic_ncu_8192_tokens": _profiled_traffic("store_kv_vec16_config4_8192tok.md"),
             "peak_source": f"hbm_gbs of {src}", "rows": res}
 
 
@@ -768,6 +773,7 @@ def measure_varlen(device, layers: int = LAYERS, reps: int = 10):
     del k, v
     return {"workload": "direct prefill, 8 x 512 + 24 x U[1,64] tokens, 16q/8kv, D128, bf16",
             "kernel": "prefill_tc2_kernel (dense mode)", "us_per_layer": round(ms * 1e3, 2),
+            "traffic_ncu": _profiled_traffic("prefill_tc2_direct_config3_sized.md"),
             "flops_per_layer": flops, "tflops": round(tfl, 1),
             "tensor_frac": round(tfl / peaks["bf16_tflops"], 4),
             "peak_source": f"bf16_tflops of {src}",
