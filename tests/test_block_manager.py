@@ -1,27 +1,82 @@
-"""Host-side page bookkeeping with copy-on-write (worker/block_manager.py).
+"""Host-side page allocator (worker/block_manager.py): the reference block
+manager's prefix cache, replayed on a recorded trace, plus copy-on-write.
 
-The reference block manager never shares a partial block, so these cases have no
-reference fixture; the checks are the allocator's invariants and, end to end on
-the CPU oracle, that a forked sequence writing into a shared partial page leaves
-the other sequence's attention exactly as it was.
+The trace (``tests/golden/block_trace.py``) was recorded from the reference
+``BlockManager`` itself (``tests/golden/make_block_golden.py``); every record
+(reuse counts, block tables, free pages, stats) must match.  Copy-on-write has
+no reference counterpart (the reference never shares a partial page), so those
+cases check the allocator's invariants and, on the CPU oracle, that a forked
+sequence writing into a shared partial page leaves the other's attention as it
+was.
 """
+import json
+
 import numpy as np
 import pytest
 
 from microinfer_b200.worker.block_manager import CowBlockManager
 from oracle import paged_oracle as po
+from tests.conftest import GOLDEN
+from tests.golden.block_trace import TraceSequence, run_trace
 
 
-class Seq:
-    def __init__(self, num_tokens):
-        self.num_tokens = num_tokens
-        self.block_table = []
+def Seq(num_tokens, block_size=16, first=1):
+    s = TraceSequence(list(range(first, first + num_tokens)))
+    s.block_size = block_size
+    return s
+
+
+@pytest.mark.parametrize("seed", ["0", "1", "2"])
+def test_trace_matches_the_reference_block_manager(seed):
+    trace = json.loads((GOLDEN / "block_manager_trace.json").read_text())[seed]
+    got = run_trace(CowBlockManager(trace["pages"], 4), TraceSequence, int(seed), trace["steps"])
+    want = trace["records"]
+    assert len(got) == len(want)
+    for i, (g, w) in enumerate(zip(got, want)):
+        assert g == w, f"record {i} differs: ours {g}, reference {w}"
+
+
+def test_prefix_hits_are_checked_by_tokens_and_never_take_the_last_page():
+    m = CowBlockManager(8, 4)
+    a = Seq(10, 4)  # pages [1-4] [5-8] [9-10]
+    assert m.can_allocate(a) == 0
+    m.allocate(a, 0)
+    a.num_scheduled_tokens = 10
+    m.hash_blocks(a)  # publishes the two full pages
+    a.num_cached_tokens, a.num_scheduled_tokens = 10, 0
+    b = Seq(9, 4)  # same first 8 tokens, then its own 9th
+    assert m.can_allocate(b) == 2
+    m.allocate(b, 2)
+    assert b.block_table[:2] == a.block_table[:2] and b.num_cached_tokens == 8
+    assert m.ref_count[a.block_table[0]] == 2 and b.block_table[2] != a.block_table[2]
+    c = Seq(8, 4)  # exactly two full pages: the last is never reused
+    assert m.can_allocate(c) == 1
+    d = Seq(10, 4, first=2)  # different tokens: no hit
+    assert m.can_allocate(d) == 0
+    assert m.stats()["prefix_cache_hit_blocks"] == 2
+
+
+def test_may_append_copies_a_shared_write_page():
+    """The scheduler's convention: before a decode step the token at num_tokens - 1
+    is the one stored; a fork shares the partial page it goes to."""
+    m = CowBlockManager(8, 4)
+    a = Seq(6, 4)
+    m.allocate(a, 0)
+    b = Seq(6, 4)
+    m.fork(a, b)
+    for s in (a, b):  # each samples its own 7th token
+        s.append_token(100 + len(s.block_table))
+    assert m.can_append(b)
+    m.may_append(b)
+    assert b.block_table[1] != a.block_table[1] and b.block_table[0] == a.block_table[0]
+    m.may_append(a)  # a is alone on the old page now: no copy
+    assert m.take_copies() == [(a.block_table[1], b.block_table[1])]
 
 
 def test_allocate_fork_free_balance():
     m = CowBlockManager(8, 16)
     a = Seq(20)  # 2 pages, the second partial
-    m.allocate(a)
+    m.allocate(a, 0)
     assert m.num_free_blocks == 6 and [m.ref_count[b] for b in a.block_table] == [1, 1]
     b = Seq(20)
     m.fork(a, b)
@@ -35,7 +90,7 @@ def test_allocate_fork_free_balance():
 def test_append_into_shared_partial_page_copies_once():
     m = CowBlockManager(8, 16)
     a = Seq(20)
-    m.allocate(a)
+    m.allocate(a, 0)
     b = Seq(20)
     m.fork(a, b)
     shared = a.block_table[1]
@@ -54,7 +109,7 @@ def test_append_into_shared_partial_page_copies_once():
 def test_append_at_page_boundary_takes_a_fresh_page():
     m = CowBlockManager(4, 16)
     a = Seq(16)
-    m.allocate(a)
+    m.allocate(a, 0)
     b = Seq(16)
     m.fork(a, b)
     slot = m.prepare_append(b)  # position 16 starts page 1: nothing to copy
@@ -65,7 +120,7 @@ def test_append_at_page_boundary_takes_a_fresh_page():
 def test_exclusive_partial_page_needs_no_copy():
     m = CowBlockManager(4, 16)
     a = Seq(5)
-    m.allocate(a)
+    m.allocate(a, 0)
     assert m.prepare_append(a) == a.block_table[0] * 16 + 5
     assert m.take_copies() == []
 
@@ -73,7 +128,7 @@ def test_exclusive_partial_page_needs_no_copy():
 def test_queued_copy_pins_its_source_until_issued():
     m = CowBlockManager(3, 16)
     a = Seq(4)
-    m.allocate(a)
+    m.allocate(a, 0)
     b = Seq(4)
     m.fork(a, b)
     src = a.block_table[0]
@@ -88,7 +143,7 @@ def test_queued_copy_pins_its_source_until_issued():
 def test_freed_destination_drops_its_copy():
     m = CowBlockManager(3, 16)
     a = Seq(4)
-    m.allocate(a)
+    m.allocate(a, 0)
     b = Seq(4)
     m.fork(a, b)
     m.prepare_append(b)
@@ -100,7 +155,7 @@ def test_freed_destination_drops_its_copy():
 def test_fork_with_queued_copies_is_refused_and_pool_exhaustion_raises():
     m = CowBlockManager(2, 16)
     a = Seq(4)
-    m.allocate(a)
+    m.allocate(a, 0)
     b = Seq(4)
     m.fork(a, b)
     m.prepare_append(b)
@@ -126,7 +181,7 @@ def test_forked_sequences_attend_to_their_own_tokens_on_the_oracle():
     vc = np.zeros_like(kc)
     m = CowBlockManager(nb, bs)
     a = Seq(20)
-    m.allocate(a)
+    m.allocate(a, 0)
     hist_k = rng.standard_normal((20, hkv, d)).astype(np.float32)
     hist_v = rng.standard_normal((20, hkv, d)).astype(np.float32)
     for pos in range(20):

@@ -218,10 +218,12 @@ def test_fused_store_with_only_the_new_token(width, split_k, early_kv):
     torch.testing.assert_close(vc[table[:, 0].long(), 0], vn, atol=0, rtol=0)
 
 
-class _Seq:
-    def __init__(self, num_tokens):
-        self.num_tokens = num_tokens
-        self.block_table = []
+def _Seq(num_tokens, block_size=16):
+    from tests.golden.block_trace import TraceSequence
+
+    s = TraceSequence(list(range(1, num_tokens + 1)))
+    s.block_size = block_size
+    return s
 
 
 def test_forked_sequences_copy_on_write_then_decode_in_isolation():
@@ -234,7 +236,7 @@ def test_forked_sequences_copy_on_write_then_decode_in_isolation():
     cache = mi.KVCache(layers, nb, bs, hkv, d, dtype=torch.bfloat16, device="cuda")
     m = mi.CowBlockManager(nb, bs)
     a = _Seq(20)
-    m.allocate(a)
+    m.allocate(a, 0)
     hist = [(torch.randn(20, hkv, d, generator=gen, device="cuda").to(torch.bfloat16),
              torch.randn(20, hkv, d, generator=gen, device="cuda").to(torch.bfloat16))
             for _ in range(layers)]
