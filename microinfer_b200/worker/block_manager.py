@@ -41,6 +41,52 @@ import numpy as np
 import xxhash
 
 
+class _Page:
+    """A view of one page's bookkeeping with the reference ``Block``'s fields
+    (``block_id``, ``ref_count``, ``hash``, ``token_ids``, ``last_used``,
+    ``update``, ``reset``), reading and writing the manager's arrays."""
+
+    __slots__ = ("_m", "block_id")
+
+    def __init__(self, manager: "CowBlockManager", block_id: int):
+        self._m = manager
+        self.block_id = block_id
+
+    @property
+    def ref_count(self) -> int:
+        return self._m.ref_count[self.block_id]
+
+    @ref_count.setter
+    def ref_count(self, value: int):
+        self._m.ref_count[self.block_id] = value
+
+    @property
+    def hash(self) -> int:
+        return self._m._key[self.block_id]
+
+    @hash.setter
+    def hash(self, value: int):
+        self._m._key[self.block_id] = value
+
+    @property
+    def token_ids(self) -> list[int]:
+        return self._m._tokens[self.block_id]
+
+    @token_ids.setter
+    def token_ids(self, value):
+        self._m._tokens[self.block_id] = value
+
+    @property
+    def last_used(self) -> int:
+        return self._m._last_used[self.block_id]
+
+    def update(self, hash: int, token_ids: list[int]):
+        self.hash, self.token_ids = hash, token_ids
+
+    def reset(self):
+        self.ref_count, self.hash, self.token_ids = 1, -1, []
+
+
 class CowBlockManager:
     def __init__(self, num_blocks: int, block_size: int):
         if type(num_blocks) is not int or type(block_size) is not int or min(num_blocks, block_size) <= 0:
@@ -69,6 +115,13 @@ class CowBlockManager:
     @property
     def free_block_ids(self) -> set[int]:
         return self._free
+
+    @property
+    def blocks(self) -> list[_Page]:
+        """Per-page views with the reference ``Block`` fields (diagnostics and tests)."""
+        if getattr(self, "_pages", None) is None:
+            self._pages = [_Page(self, i) for i in range(self.num_blocks)]
+        return self._pages
 
     @property
     def num_free_blocks(self) -> int:

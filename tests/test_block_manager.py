@@ -9,7 +9,11 @@ cases check the allocator's invariants and, on the CPU oracle, that a forked
 sequence writing into a shared partial page leaves the other's attention as it
 was.
 """
+import importlib.util
+import inspect
 import json
+import sys
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -214,3 +218,52 @@ def test_forked_sequences_attend_to_their_own_tokens_on_the_oracle():
             p = np.exp(s - s.max())
             want[h] = (p / p.sum()) @ vals[:, h // g]
         np.testing.assert_allclose(out[i], want, rtol=1e-5, atol=1e-5)
+
+
+REF_TESTS = Path("/root/reference/tests/engine/test_blockmanager.py")
+
+
+def _reference_block_manager_tests():
+    """(name, function, kwargs) for every case of the reference's own block-manager
+    tests, parametrize marks expanded; empty when the reference tree is absent."""
+    if not REF_TESTS.exists():
+        return []
+    ref_pkg = Path(__file__).resolve().parent.parent / "baseline" / "_ref"
+    for p in (str(ref_pkg), "/root/reference"):
+        if p not in sys.path:
+            sys.path.append(p)  # after this repository: its tests package must not shadow ours
+    spec = importlib.util.spec_from_file_location("reference_test_blockmanager", REF_TESTS)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    mod.BlockManager = CowBlockManager  # the module's tests now build our manager
+    cases = []
+    for name in sorted(n for n in vars(mod) if n.startswith("test_")):
+        if name == "test_block_reset_discards_previous_content":
+            continue  # a test of the reference's Block class itself
+        fn = getattr(mod, name)
+        grids = [({},)]
+        for mark in getattr(fn, "pytestmark", []):
+            if mark.name == "parametrize":
+                names = [a.strip() for a in mark.args[0].split(",")]
+                vals = [v if len(names) > 1 else (v,) for v in mark.args[1]]
+                grids.append(tuple(dict(zip(names, v)) for v in vals))
+        combos = [{}]
+        for grid in grids:
+            combos = [dict(c, **g) for c in combos for g in grid]
+        cases += [(f"{name}{sorted(c.items())}", fn, c) for c in combos]
+    return cases
+
+
+@pytest.mark.parametrize("case", _reference_block_manager_tests(), ids=lambda c: c[0])
+def test_reference_block_manager_tests_pass_on_ours(case, monkeypatch):
+    """The reference's tests/engine/test_blockmanager.py, unchanged, with its
+    BlockManager replaced by CowBlockManager and its sequence_cls fixture (the
+    reference Sequence with block size 4)."""
+    from microinfer.engine.sequence import Sequence
+
+    monkeypatch.setattr(Sequence, "block_size", 4)
+    _, fn, kwargs = case
+    params = inspect.signature(fn).parameters
+    if "sequence_cls" in params:
+        kwargs = dict(kwargs, sequence_cls=Sequence)
+    fn(**kwargs)
