@@ -1564,9 +1564,10 @@ def run_ours(args):
             "config": bench_config(world),
             "plan": {"split_k": split, "decode_kernel": decode_kernel,
                      "bytes_per_step_per_gpu": step_bytes,
-                     "graph": "one CUDA graph per step: 28 store+decode launches, the sampler "
-                              "and (N > 1) the previous step's token all_gather on a side "
-                              "branch"},
+                     "graph": "one CUDA graph per step: 28 store+decode launches and the "
+                              "sampler; with N > 1 the step's token all_gather is a second "
+                              "captured graph replayed on a side stream after it, overlapping "
+                              "the next step's layers"},
             "tok_per_s": round(world * NSEQ / (ms_step * 1e-3), 1),
             "median_step_ms": round(statistics.median(per_step), 5),
             "rank_ms_per_step": rank_ms,
