@@ -379,23 +379,31 @@ __global__ void __launch_bounds__(kThreads2, 1)
       uint32_t items_q = 0;
       uint32_t fixes[kVStages] = {0, 0};  // fix-ups consumed per V ring slot
       bool ok = true;
+      // Descriptors are built once; a K step or a ring slot only moves the start
+      // address field (bits 0-13, in 16-byte units), so each MMA's operands are a
+      // base plus a constant: this lone thread shares its SM sub-partition with two
+      // busy softmax warps, and every issue slot it spends delays the tensor pipe.
+      const uint64_t qd0 = kmajor_desc(sQ, 0), kd0 = kmajor_desc(sK, 0), vd0 = mnmajor_desc(sV, 0);
+      constexpr uint64_t kTile16 = kTileBytes >> 4;
+      auto kstep = [](int kk) -> uint64_t {  // K-major offset of K step kk, 16-byte units
+        return static_cast<uint64_t>(((kk >> 2) * kHalf + (kk & 3) * 32) >> 4);
+      };
       auto s_mma = [&](int x) {  // S_X = Q_X K^T with the K tile at ring position kt
-        const uint32_t ks = kt % kKStages;
+        const uint64_t qd = qd0 + x * kTile16, kd = kd0 + (kt % kKStages) * kTile16;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          tc::umma_f16(tmem + x * 128, kmajor_desc(sQ + x * kTileBytes, kk),
-                       kmajor_desc(sK + ks * kTileBytes, kk), kIdescQK, kk > 0 ? 1u : 0u);
+          tc::umma_f16(tmem + x * 128, qd + kstep(kk), kd + kstep(kk), kIdescQK, kk > 0 ? 1u : 0u);
         tc::umma_commit(&bar[C_SFULL + x]);
         ++sc[x];
       };
       auto pv_mma = [&](int x, int j) -> bool {  // O_X += P_X(j) V_j, P from TMEM
         if (!mbar_spin_bounded(&bar[C_PFULL + x], (sc[x] - 1) & 1, p.status)) return false;
         tc::fence_after_sync();
+        const uint64_t vd = vd0 + (vt % kVStages) * kTile16;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          tc::umma_f16_tmem_a(tmem + 256 + x * 128, tmem + x * 128 + kk * 8,
-                              mnmajor_desc(sV + (vt % kVStages) * kTileBytes, kk), kIdescPV,
-                              (j > 0 || kk > 0) ? 1u : 0u);
+          tc::umma_f16_tmem_a(tmem + 256 + x * 128, tmem + x * 128 + kk * 8, vd + kk * (2048 >> 4),
+                              kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
         return true;
       };
       for (int64_t idx = blockIdx.x; idx < n_items && ok; idx += gridDim.x) {
