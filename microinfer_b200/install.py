@@ -113,7 +113,6 @@ def install(package: str = "microinfer") -> dict:
     rebind(cached, "paged_attention_meta", _pa.paged_attention_meta)
     rebind(cached, "flash_attn_varlen_func", flash_attn_varlen_compat)
     rebind(cached, "_direct_prefill_flash", direct_prefill_compat)
-    sys.modules.setdefault("microinfer_b200.installed_into", kv_cache)
     return replaced
 
 
