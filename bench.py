@@ -33,6 +33,10 @@ sys.path.insert(0, str(ROOT))
 
 LAYERS, HQ, HKV, D, BS, NB, NSEQ = 28, 16, 8, 128, 16, 1024, 8
 E2E_GROUP = 7  # layers per input copy on the end-to-end path
+# Sampled-token buffers in flight with N > 1 (step k reuses slot k % n once the
+# gather that read it is done); one GPU has no gather and keeps two.  (8 GPUs, 200
+# steps: 0.206 ms per step with 4, 0.222 with 32.)
+TOKEN_SLOTS = 4
 # Whole-step graph of the end-to-end path: inputs go in as runs of layers ending at
 # E2E_IN_ENDS (a one-layer first run, so layer 0 waits for 64 KB only), outputs come back as
 # runs ending at E2E_OUT_ENDS (a one-layer last run).  On B200 this beat groups of 7 both ways
@@ -1284,10 +1288,11 @@ def run_ours(args):
     vn = list(pk_d[:, qn + kvn:].unflatten(1, (NSEQ, HKV, D)).unbind(0))
     del q_all, kn_all, vn_all
     out = torch.empty(LAYERS, NSEQ, HQ, D, dtype=torch.bfloat16, device=device)
-    # Sampled token ids, double-buffered: step k writes buffer k % 2 while the
-    # all_gather of step k-1 (off the attention path, on its own stream) reads
-    # the other one.
-    tokens_buf = torch.empty(2, NSEQ, dtype=torch.int32, device=device)
+    # Sampled token ids in a ring of n_slots buffers: step k writes buffer
+    # k % n_slots while the all_gathers of the steps before it (off the attention
+    # path, on their own stream) read the others.
+    n_slots = TOKEN_SLOTS if world > 1 else 2
+    tokens_buf = torch.empty(n_slots, NSEQ, dtype=torch.int32, device=device)
     tokens = tokens_buf[0]
     decode_kernel, split, _ = mi.decode_plan(NSEQ, HQ, HKV, D, torch.bfloat16, BS, 0, device,
                                              table_d.shape[1])
@@ -1322,21 +1327,21 @@ def run_ours(args):
     torch.cuda.current_stream(device).wait_stream(stream)
     torch.cuda.synchronize(device)
     cur = torch.cuda.current_stream(device)
-    gathered = torch.empty(2, world * NSEQ, dtype=torch.int32, device=device)
+    gathered = torch.empty(n_slots, world * NSEQ, dtype=torch.int32, device=device)
     ag_stream = torch.cuda.Stream(device)
     if world > 1:  # communicators exist before any capture
         dist.all_gather_into_tensor(gathered[0], tokens_buf[0])
         torch.cuda.synchronize(device)
-    # One CUDA graph per step, double-buffered on the token slot: graph `slot` runs the
-    # 28 layers and the sampler into tokens_buf[slot].  With N > 1 the NCCL all_gather of
-    # those token ids (for the scheduler; the attention never waits on it) is a second
-    # captured graph, replayed on its own stream once the step's graph is done, so it
-    # overlaps the next step's layers; step k + 2 reuses the slot only after that gather.
+    # One CUDA graph per token slot: graph `slot` runs the 28 layers and the sampler into
+    # tokens_buf[slot].  With N > 1 the NCCL all_gather of those token ids (for the
+    # scheduler; the attention never waits on it) is a second captured graph, replayed on
+    # its own stream once the step's graph is done, so it overlaps the next steps' layers;
+    # step k + n_slots reuses the slot only after that gather.
     # The host issues two graph launches and three event operations per step.  (Measured
     # at N = 2: 0.1604 ms per step this way, 0.1648 with the gather as a side branch inside
     # the step's graph, 0.1734 with it at the end of the graph, 0.1592 with no gather.)
     graphs, ag_graphs = [], []
-    for slot in range(2):
+    for slot in range(n_slots):
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr):
             layer_loop(slot)
@@ -1353,11 +1358,11 @@ def run_ours(args):
     dgraph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(dgraph):
         decode_only()
-    ag_ready = [torch.cuda.Event() for _ in range(2)]
-    ag_done = [torch.cuda.Event() for _ in range(2)]
+    ag_ready = [torch.cuda.Event() for _ in range(n_slots)]
+    ag_done = [torch.cuda.Event() for _ in range(n_slots)]
 
     def step(k):
-        slot = k & 1
+        slot = k % n_slots
         if world > 1:
             cur.wait_event(ag_done[slot])
         graphs[slot].replay()
@@ -1372,7 +1377,7 @@ def run_ours(args):
         if world > 1:
             cur.wait_stream(ag_stream)
 
-    warm = max(3, args.warmup)
+    warm = max(3, args.warmup, n_slots)  # every slot's graphs replayed before timing
     for k in range(warm):
         step(k)
     last_gather(warm - 1)
@@ -1408,12 +1413,15 @@ def run_ours(args):
     gaps = [ends[k].elapsed_time(starts[k + 1]) for k in range(args.steps - 1)]
     ms_step = total_ms / args.steps
     gap_stats = [statistics.median(gaps) * 1e3 if gaps else 0.0, max(gaps) * 1e3 if gaps else 0.0]
+    ordered = sorted(per_step)
+    step_dist = [ordered[len(ordered) // 2], ordered[(9 * len(ordered)) // 10], ordered[-1]]
     if world > 1:
-        t = torch.tensor([ms_step, gap_stats[0], gap_stats[1]], device=device)
+        t = torch.tensor([ms_step, gap_stats[0], gap_stats[1], *step_dist], device=device)
         every = [torch.empty_like(t) for _ in range(world)]
         dist.all_gather(every, t)
         ms_step = max(float(x[0]) for x in every)
         gap_stats = [max(float(x[1]) for x in every), max(float(x[2]) for x in every)]
+        step_dist = [max(float(x[3 + i]) for x in every) for i in range(3)]
         rank_ms = [round(float(x[0]), 5) for x in every]
     else:
         rank_ms = [round(ms_step, 5)]
@@ -1558,7 +1566,7 @@ def run_ours(args):
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms_step, 5),
+            "steps": args.steps, "warmup": warm, "ms_per_step": round(ms_step, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded torch, BASELINE configs[1] shapes), random-init pool",
             "config": bench_config(world),
@@ -1571,6 +1579,9 @@ def run_ours(args):
             "tok_per_s": round(world * NSEQ / (ms_step * 1e-3), 1),
             "median_step_ms": round(statistics.median(per_step), 5),
             "rank_ms_per_step": rank_ms,
+            "step_ms": {"median": round(step_dist[0], 5), "p90": round(step_dist[1], 5),
+                        "max": round(step_dist[2], 5),
+                        "what": "device time of single steps (a step's event pair), max over ranks"},
             "step_gap_us": {"median": round(gap_stats[0], 2), "max": round(gap_stats[1], 2),
                             "what": "device idle time between one step's end and the next "
                                     "step's start, max over ranks"},
