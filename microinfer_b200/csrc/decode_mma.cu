@@ -193,13 +193,9 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
   const bool fused = p.k_new != nullptr;
 
   if (lane == 0) {
-#pragma unroll
-    for (int s = 0; s < kStagesM; ++s) mbar_init(&wbar[s], 1);
-    fence_mbar_init();
     tc::prefetch_tmap(&P.tmap_k);
     tc::prefetch_tmap(&P.tmap_v);
   }
-  __syncwarp();
 
   // Without early_kv everything below may come from the preceding kernel (a
   // mixed-batch launch needs no wait: see DecodeParams::cu_q).
@@ -234,6 +230,14 @@ __global__ void __launch_bounds__(kWarpsM * 32, 1)
   };
   int ctx = mixed ? __ldg(p.cu_k + seq + 1) - __ldg(p.cu_k + seq) : __ldg(p.context_lens + seq);
   const int64_t slot = fused ? static_cast<int64_t>(__ldg(p.slot_mapping + seq)) : -1;
+  // The ring's barriers are set up while those reads (the kernel's first global
+  // accesses: context length, slot, block-table entries) are in flight.
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < kStagesM; ++s) mbar_init(&wbar[s], 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
   const int64_t cap = p.bt_stride * p.block_size;
   if (ctx > cap) {
     if (threadIdx.x == 0 && split == 0) flag_status(p.status, MI_DEV_BAD_BLOCK);
