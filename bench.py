@@ -1197,18 +1197,25 @@ def _e2e_whole_step_graph(device, cur, in_ends, out_ends, attention_layers, samp
     cuts = sorted(set(in_ends) | set(out_ends))
     assert cuts[-1] == LAYERS and in_ends[-1] == LAYERS and out_ends[-1] == LAYERS
     h2d_s, d2h_s = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    # the step's metadata and the token read-back each get a copy stream of their own,
+    # so they run beside the first input run and the last output run, not after them
+    meta_s, tok_s = torch.cuda.Stream(device), torch.cuda.Stream(device)
     ev_in = {e: torch.cuda.Event() for e in in_ends}
     ev_done = {e: torch.cuda.Event() for e in out_ends}
+    ev_meta, ev_tok = torch.cuda.Event(), torch.cuda.Event()
     sg = torch.cuda.CUDAGraph()
     with torch.cuda.graph(sg):
         cs = torch.cuda.current_stream(device)
         h2d_s.wait_stream(cs)
-        _copy_async(meta_d, h_meta, h2d_s)
+        meta_s.wait_stream(cs)
+        _copy_async(meta_d, h_meta, meta_s)
+        ev_meta.record(meta_s)
         lo = 0
         for e in in_ends:
             _copy_async(pk_d[lo:e], h_pk[lo:e], h2d_s)
             ev_in[e].record(h2d_s)
             lo = e
+        cs.wait_event(ev_meta)
         lo, out_lo = 0, 0
         for hi in cuts:
             starts = [e for e in in_ends if e > lo]
@@ -1216,20 +1223,22 @@ def _e2e_whole_step_graph(device, cur, in_ends, out_ends, attention_layers, samp
                 cs.wait_event(ev_in[starts[0]])
             attention_layers(range(lo, hi))
             if hi == LAYERS:
-                sample()
-                tok_all.copy_(tokens)
+                sample()  # one GPU: the gathered token ids are this GPU's own
+                ev_tok.record(cs)
+                tok_s.wait_event(ev_tok)
+                _copy_async(h_tok, tokens, tok_s)
             if hi in out_ends:
                 ev_done[hi].record(cs)
                 d2h_s.wait_event(ev_done[hi])
                 _copy_async(h_out[out_lo:hi], out[out_lo:hi], d2h_s)
                 out_lo = hi
             lo = hi
-        _copy_async(h_tok, tok_all, d2h_s)
         cs.wait_stream(d2h_s)
+        cs.wait_stream(tok_s)
     for _ in range(3):
         sg.replay()
     torch.cuda.synchronize(device)
-    if not (torch.equal(h_out, out.cpu()) and torch.equal(h_tok, tok_all.cpu())):
+    if not (torch.equal(h_out, out.cpu()) and torch.equal(h_tok, tokens.cpu())):
         raise RuntimeError("whole-step graph read-back differs from the device results")
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     x0.record(cur)
